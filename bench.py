@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Benchmark: Cut Cross-Entropy forward+backward tokens/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3] [--impl ours|reference]
+
+One step = forward + backward of the fused linear + cross-entropy over one
+batch of the synthetic workload (default: config 3, the Llama-3.1-8B head,
+N=4096 tokens, D=4096, V=128256, bf16, peaked logits, Zipf targets, 5%
+ignored, reduction='mean'), producing grad_e and grad_c.  With N GPUs (one
+process per GPU under torchrun) the vocabulary is split across the ranks
+(strong scaling: the same N tokens per step, V/N classifier rows per GPU);
+the per-row statistics are all-gathered and grad_e all-reduced over NCCL.
+
+Prints ONE JSON line on rank 0.  ``--impl reference`` times the CPU
+restatement of the reference's pure-MLX path (oracle/cce_oracle.py) on the
+host cores instead, on a bounded row sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "mlx-cross-entropy_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "CCE fwd+bwd tokens/s (Llama-3-8B head, bf16) and % of BF16 tensor peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                idx = int(r[0])
+            except ValueError:
+                continue
+            if idx not in gpus:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except ValueError:
+                pass
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        busy = [s for s in sm if s > 0.5 * max(sm)]
+        return {"sm_mhz": statistics.median(busy or sm), "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU restatement of the reference's pure-MLX path
+# ---------------------------------------------------------------------------
+
+def cpu_reference_step_fn(cfg, rows):
+    """Returns (step(), sample description, cores) timing the oracle on a row sample."""
+    sys.path.insert(0, str(REPO))
+    from oracle import cce_oracle as O
+    from mlx_cce import synthetic
+    e, c, t, bias, go, w = synthetic.make_inputs(cfg)
+    e2 = e.reshape(-1, w.D)[:rows].float().numpy()
+    t2 = t.reshape(-1)[:rows].numpy()
+    c32 = c.float().numpy()
+    b32 = None if bias is None else bias.float().numpy()
+    red = w.reduction if w.reduction != "none" else "sum"
+
+    def step():
+        O.cpu_fwd_bwd_step(e2, c32, t2, b32, reduction=red)
+
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count() or 1
+    sample = (f"first {rows} of {w.N} rows of config {cfg} against the full V={w.V} x D={w.D} "
+              f"classifier: chunked online-LSE forward + analytic dE/dC backward, float32 numpy")
+    return step, sample, cores, w
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    rows = args.ref_rows
+    step, sample, cores, w = cpu_reference_step_fn(args.config, rows)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = rows / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"cfg{w.cfg} {w.name}", "N": w.N, "D": w.D, "V": w.V,
+                   "global_batch": w.N, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "MLX is not installable here: the reference's pure-MLX path is timed through its "
+                "CPU restatement (oracle/cce_oracle.py).",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import torch.distributed as dist
+    import mlx_cce
+    from mlx_cce import _ext, synthetic
+    from mlx_cce import distributed as mdist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    e_cpu, c_cpu, t_cpu, b_cpu, go_cpu, w = synthetic.make_inputs(args.config)
+    N, D, V = w.N, w.D, w.V
+    v0, v1 = mdist.vocab_shard(V, rank, world)
+    e_cpu = e_cpu.reshape(N, D)
+    t_cpu = t_cpu.reshape(N)
+    e = e_cpu.to(dev)
+    t = t_cpu.to(dev)
+    c = c_cpu[v0:v1].contiguous().to(dev).requires_grad_(True)
+    bias = b_cpu[v0:v1].contiguous().to(dev).requires_grad_(True) if b_cpu is not None else None
+    go = go_cpu.reshape(N).to(dev) if go_cpu is not None else None
+    del c_cpu
+    skip = torch.zeros(2, dtype=torch.int64, device=dev)
+
+    def step(e_in, t_in):
+        e_in = e_in.detach().requires_grad_(True)
+        c.grad = None
+        if bias is not None:
+            bias.grad = None
+        if world > 1:
+            loss = mdist.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
+                                              v_offset=v0, skip_stats=skip)
+        else:
+            loss = mlx_cce.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
+                                                skip_stats=skip)
+        if w.reduction == "none":
+            loss.backward(go)
+        else:
+            loss.backward()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        tt = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    for _ in range(args.warmup):
+        step(e, t)
+    barrier()
+
+    # ---- device-resident timed region ----
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    skip.zero_()
+    launches0 = _ext.launch_count()
+    _ext.set_timing(True)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step(e, t)
+    ev1.record()
+    torch.cuda.synchronize()
+    elapsed_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    launches = _ext.launch_count() - launches0
+    recs = _ext.timings()
+    _ext.set_timing(False)
+    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+    fwd_ms = [a.elapsed_time(b) for name, a, b in recs if name == "forward"]
+    bwd_ms = [a.elapsed_time(b) for name, a, b in recs if name == "backward"]
+    fwd_avg = max_over_ranks(statistics.mean(fwd_ms)) if fwd_ms else float("nan")
+    bwd_avg = max_over_ranks(statistics.mean(bwd_ms)) if bwd_ms else float("nan")
+    skipped, total = skip.tolist()
+
+    # ---- end-to-end through the public API with host buffers ----
+    e_host = e_cpu.pin_memory()
+    t_host = t_cpu.pin_memory()
+    e_dev = torch.empty_like(e)
+    t_dev = torch.empty_like(t)
+    barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev2.record()
+    d2h = 0
+    for _ in range(args.steps):
+        e_dev.copy_(e_host, non_blocking=True)
+        t_dev.copy_(t_host, non_blocking=True)
+        loss = step(e_dev, t_dev)
+        host = loss.detach().cpu()
+        d2h = host.numel() * host.element_size()
+    ev3.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
+    h2d = e_host.numel() * e_host.element_size() + t_host.numel() * t_host.element_size()
+
+    # ---- CPU baseline (rank 0 at N=1 only) ----
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        stepc, sample, cores, _ = cpu_reference_step_fn(args.config, args.ref_rows)
+        stepc()  # warm-up
+        t0 = time.perf_counter()
+        stepc()
+        dtc = time.perf_counter() - t0
+        cpu = {"value": args.ref_rows / dtc, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        peaks, src = load_peaks()
+        ms = elapsed_ms / args.steps
+        value = N / (ms / 1e3)
+        flops = 8.0 * N * V * D
+        tflops = flops / (ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        peak_burst = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        vl = v1 - v0
+        fwd_tflops = 2.0 * N * vl * D / (fwd_avg / 1e3) / 1e12
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else str(w.dtype),
+            "data": "synthetic (seeded, see mlx_cce/synthetic.py)",
+            "config": {"workload": f"cfg{w.cfg} {w.name}", "N": N, "D": D, "V": V,
+                       "global_batch": N, "seq_len": w.batch[-1] if len(w.batch) > 1 else N,
+                       "reduction": w.reduction,
+                       "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (c is %.2f GB), no flush" % (V * D * 2 / 1e9)},
+            "tflops": tflops, "pct_bf16_peak": tflops / peak_burst,
+            "pct_bf16_peak_sustained": tflops / peak,
+            "flops_per_step": flops,
+            "skipped_blocks_frac": (skipped / total) if total else None,
+            "fwd_ms": fwd_avg, "bwd_ms": bwd_avg,
+            "roofline": {"bound": "tensor", "kernel": "forward (logits + online LSE)",
+                         "achieved": fwd_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": fwd_tflops / peak, "peak_kind": f"{src} bf16 sustained",
+                         "traffic": None},
+            "e2e": {"value": N * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-rows", type=int, default=256,
+                    help="rows of the workload in one CPU-reference step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: --warmup below 3 does not meet the timing rules", file=sys.stderr)
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,163 @@
+/*
+ * cce_b200.h -- C ABI of the B200 (sm_100a) Cut Cross-Entropy library.
+ *
+ * This ABI replaces the nanobind module of the reference
+ * (csrc/bindings.cpp:12-87) and the MLX primitives behind it
+ * (csrc/cce/cce.h:10-101, csrc/cce/cce.cpp:123-375).  Everything crossing it
+ * is a plain pointer or integer: no torch, no MLX, no C++ types, and no
+ * exception ever crosses it.
+ *
+ * Conventions
+ *   - Every tensor pointer is DEVICE memory on the current CUDA device,
+ *     contiguous and row-major.  The caller allocates every input, output
+ *     and workspace; the library never calls cudaMalloc on these paths.
+ *   - ``stream`` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  All work is enqueued asynchronously on it.
+ *   - Return value: CCE_OK (0) or a negative CCE_ERR_* code; the message is in
+ *     cce_last_error() (thread-local, valid until the next call on the thread).
+ *   - Rows: N flattened tokens.  D: hidden size.  V: number of vocabulary rows
+ *     of ``c`` handled by THIS call (a shard of the full vocabulary when the
+ *     vocabulary is split across ranks); global vocab id = v_offset + local id.
+ *   - targets are int32, already sanitised (ignored rows replaced by 0, as in
+ *     mlx_cce/__init__.py:59-64 of the reference), with values in
+ *     [0, V_total).  A target outside [v_offset, v_offset + V) is "not on this
+ *     shard" and contributes a target logit of 0.
+ */
+#ifndef CCE_B200_H
+#define CCE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CCE_API __attribute__((visibility("default")))
+#else
+#define CCE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define CCE_OK             0
+#define CCE_ERR_SHAPE     -1  /* bad N / D / V / sizes                         */
+#define CCE_ERR_DTYPE     -2  /* unsupported dtype code                         */
+#define CCE_ERR_ALIGN     -3  /* pointer misaligned for the selected kernel     */
+#define CCE_ERR_CUDA      -4  /* a CUDA runtime call or launch failed           */
+#define CCE_ERR_ARCH      -5  /* device is not sm_100 (B200)                    */
+#define CCE_ERR_WORKSPACE -6  /* workspace NULL or smaller than required        */
+#define CCE_ERR_ARG       -7  /* NULL required pointer or bad flag combination  */
+
+/* dtype codes (inputs e, c; bias has its own code) */
+#define CCE_F32  0
+#define CCE_F16  1
+#define CCE_BF16 2
+
+/* Vocabulary columns summarised by one tile statistic.  tile_max is laid out
+ * [ceil(V / CCE_STAT_TILE)][N] (tile-major, rows contiguous). */
+#define CCE_STAT_TILE 128
+
+/* backward flags */
+#define CCE_NEED_DE     1   /* write grad_e                                       */
+#define CCE_NEED_DC     2   /* write grad_c                                       */
+#define CCE_NEED_DBIAS  4   /* write grad_bias (fp32)                             */
+#define CCE_DE_F32      8   /* grad_e is fp32 [N, D] (for a cross-rank sum), else e's dtype */
+#define CCE_NO_FILTER  16   /* exact gradients: never skip a block                */
+
+/* ln(2^-12): the reference's gradient-filter threshold (csrc/cce/cce.metal:143). */
+#define CCE_FILTER_LOG_EPS (-8.3177661667f)
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+CCE_API int cce_version(void);
+
+/* Thread-local message describing the last failed call on this thread. */
+CCE_API const char* cce_last_error(void);
+
+/* Number of CUDA kernels this library has launched in this process (all
+ * devices, all threads).  Instrumentation only; no counterpart in the
+ * reference. */
+CCE_API uint64_t cce_launch_count(void);
+
+/* Number of vocabulary tile statistics per row: ceil(V / CCE_STAT_TILE). */
+CCE_API int64_t cce_num_stat_tiles(int64_t V);
+
+/*
+ * Forward workspace size in bytes for cce_forward with these sizes.
+ */
+CCE_API size_t cce_forward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype);
+
+/*
+ * cce_forward -- fused logits + per-tile max / sum-exp + target logit + LSE.
+ *
+ * Replaces cce_forward_raw (csrc/bindings.cpp:58-69, csrc/cce/cce.cpp:123-145)
+ * and CutCrossEntropy::eval_gpu (csrc/cce/cce.cpp:207-277): the forward tile
+ * kernel (csrc/cce/cce.metal:19-135) followed by reduce_tile_to_lse
+ * (csrc/cce/cce.metal:332-355).  The [N, V] logits are never stored.
+ *
+ *   e        [N, D]   dtype          c [V, D] dtype
+ *   bias     [V]      bias_dtype or NULL
+ *   targets  [N]      int32 sanitised global ids
+ *   tile_max [ceil(V/128)][N] fp32 out: max logit (+bias) of each row over
+ *            each 128-column vocabulary tile (the backward's filter input)
+ *   lse      [N] fp32 out: log-sum-exp over this call's V columns
+ *   tgt      [N] fp32 out: logit (+bias) of the row's target when the target
+ *            lies in [v_offset, v_offset + V), else 0
+ *   workspace >= cce_forward_workspace_bytes(N, D, V, dtype)
+ */
+CCE_API int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
+                const int32_t* targets, int64_t N, int64_t D, int64_t V,
+                int64_t v_offset, int dtype,
+                float* tile_max, float* lse, float* tgt,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * cce_lse_combine -- merge P partial (lse, target-logit) rows into one.
+ *
+ *   part_lse, part_tgt: P rows of N fp32 values, row p starting at
+ *   part_lse + p * part_stride (e.g. gathered from P vocabulary shards).
+ *   lse[n] = log sum_p exp(part_lse[p][n]); tgt[n] = sum_p part_tgt[p][n]
+ *   (tgt nullable); nll[n] (nullable) = lse[n] - tgt[n].  The outputs may
+ *   alias no input.
+ * The per-rank fold of reduce_tile_to_lse (csrc/cce/cce.metal:332-355) lifted
+ * one level up, plus nll = lse + neg_target_logit of mlx_cce/__init__.py:32.
+ */
+CCE_API int cce_lse_combine(const float* part_lse, const float* part_tgt, int64_t P, int64_t N,
+                    int64_t part_stride, float* lse, float* tgt, float* nll, void* stream);
+
+/*
+ * Backward workspace size in bytes for cce_backward with these sizes/flags.
+ */
+CCE_API size_t cce_backward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags);
+
+/*
+ * cce_backward -- filtered recompute of softmax - onehot and the grad GEMMs.
+ *
+ * Replaces cce_backward_raw (csrc/bindings.cpp:71-86, csrc/cce/cce.cpp:152-179)
+ * and CutCrossEntropyBwd::eval_gpu (csrc/cce/cce.cpp:283-375) running the
+ * backward kernel (csrc/cce/cce.metal:146-326) with COMPUTE_DC, i.e. the
+ * compute_all_grads path of reference/_fused_backward.py:1618-1655.
+ *
+ *   lse       [N] fp32: GLOBAL log-sum-exp (after any cross-shard combine)
+ *   d_nll     [N] fp32: cotangent of each row's NLL (0 for ignored rows)
+ *   tile_max  [ceil(V/128)][N] fp32 from cce_forward
+ *   grad_e    [N, D] e's dtype, or fp32 with CCE_DE_F32 (overwritten)
+ *   grad_c    [V, D] c's dtype (overwritten; NULL unless CCE_NEED_DC)
+ *   grad_bias [V] fp32 (overwritten; NULL unless CCE_NEED_DBIAS)
+ *   skip_stats device int64[2] (nullable): accumulates (skipped, total)
+ *            (128-row x 128-column) blocks of this call
+ *   filter_log_eps: a block whose every row has tile_max - lse below it and
+ *            holds no target is skipped (CCE_FILTER_LOG_EPS = the reference's).
+ */
+CCE_API int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
+                 const int32_t* targets, const float* lse, const float* d_nll,
+                 const float* tile_max, int64_t N, int64_t D, int64_t V,
+                 int64_t v_offset, int dtype, int flags, float filter_log_eps,
+                 void* grad_e, void* grad_c, float* grad_bias, int64_t* skip_stats,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CCE_B200_H */

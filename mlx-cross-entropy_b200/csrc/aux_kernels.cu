@@ -1,0 +1,165 @@
+// Auxiliary kernels: LSE combine, backward block mask, casts.
+//
+// - lse_combine_kernel: per row, fold P partial (max, sum-exp) pairs -- the
+//   vocabulary tiles of one call, or the vocabulary shards of several ranks --
+//   into lse = M + log(sum_p s_p * exp(m_p - M)) with M = max_p m_p.  This is
+//   reduce_tile_to_lse of the reference (csrc/cce/cce.metal:332-355), with the
+//   target-logit sum and nll = lse - tgt (mlx_cce/__init__.py:32) fused in.
+// - block_mask_kernel: the reference's per-tile skip decision
+//   (csrc/cce/cce.metal:190-204) taken once per (128-row block, 128-column
+//   vocabulary tile) instead of inside the backward kernel.
+#include "kernels.cuh"
+
+namespace cce {
+
+namespace {
+
+constexpr int kCombRows = 32;    // rows per block (threadIdx.x)
+constexpr int kCombSlices = 8;   // partial slices per row (threadIdx.y)
+
+__global__ void __launch_bounds__(kCombRows * kCombSlices)
+lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__ part_sum,
+                   const float* __restrict__ part_tgt, int64_t P, int64_t N, int64_t ld,
+                   float* __restrict__ lse, float* __restrict__ tgt, float* __restrict__ nll) {
+  __shared__ float sm[kCombSlices][kCombRows];
+  __shared__ float ss[kCombSlices][kCombRows];
+  __shared__ float st[kCombSlices][kCombRows];
+  const int64_t row = (int64_t)blockIdx.x * kCombRows + threadIdx.x;
+  float m = -INFINITY, s = 0.f, t = 0.f;
+  if (row < N) {
+    for (int64_t p = threadIdx.y; p < P; p += kCombSlices) {
+      const float mp = part_max[p * ld + row];
+      const float sp = part_sum ? part_sum[p * ld + row] : 1.0f;
+      if (part_tgt) t += part_tgt[p * ld + row];
+      if (sp > 0.f) {
+        if (mp > m) {
+          s = s * exp2f((m - mp) * kLog2e) + sp;
+          m = mp;
+        } else {
+          s += sp * exp2f((mp - m) * kLog2e);
+        }
+      }
+    }
+  }
+  sm[threadIdx.y][threadIdx.x] = m;
+  ss[threadIdx.y][threadIdx.x] = s;
+  st[threadIdx.y][threadIdx.x] = t;
+  __syncthreads();
+  if (threadIdx.y == 0 && row < N) {
+    float M = -INFINITY;
+    for (int i = 0; i < kCombSlices; ++i) M = fmaxf(M, sm[i][threadIdx.x]);
+    float S = 0.f, T = 0.f;
+    for (int i = 0; i < kCombSlices; ++i) {
+      const float si = ss[i][threadIdx.x];
+      if (si > 0.f) S += si * exp2f((sm[i][threadIdx.x] - M) * kLog2e);
+      T += st[i][threadIdx.x];
+    }
+    const float L = M + logf(S);
+    lse[row] = L;
+    if (tgt) tgt[row] = T;
+    if (nll) nll[row] = L - T;
+  }
+}
+
+__global__ void __launch_bounds__(kRowBlock)
+block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ lse,
+                  const int32_t* __restrict__ targets, const float* __restrict__ d_nll, int64_t N,
+                  int64_t V, int64_t v_offset, float log_eps, int no_filter, uint8_t* __restrict__ keep,
+                  unsigned long long* __restrict__ skip_stats) {
+  const int64_t j = blockIdx.x;   // vocabulary tile
+  const int64_t i = blockIdx.y;   // row block
+  const int64_t row = i * kRowBlock + threadIdx.x;
+  const int64_t nVt = gridDim.x;
+  int k = 0;
+  if (row < N) {
+    const float g = d_nll[row];
+    if (g != 0.f) {  // rows with a zero cotangent contribute nothing
+      if (no_filter) {
+        k = 1;
+      } else {
+        const int64_t tl = (int64_t)targets[row] - v_offset;
+        const bool hit = tl >= j * kStatTile && tl < (j + 1) * kStatTile && tl < V;
+        k = hit || (tile_max[j * N + row] - lse[row] >= log_eps);
+      }
+    }
+  }
+  k = __syncthreads_or(k);
+  if (threadIdx.x == 0) {
+    keep[i * nVt + j] = (uint8_t)k;
+    if (skip_stats) {
+      atomicAdd(&skip_stats[1], 1ull);
+      if (!k) atomicAdd(&skip_stats[0], 1ull);
+    }
+  }
+}
+
+template <typename T>
+__global__ void cast_f32_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = from_f32<T>(src[i]);
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = v;
+}
+
+int grid_for(int64_t n, int threads) {
+  int64_t b = ceil_div(n, threads);
+  if (b > 148 * 16) b = 148 * 16;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace
+
+cudaError_t launch_lse_combine(const float* part_max, const float* part_sum, const float* part_tgt,
+                               int64_t P, int64_t N, int64_t ld, float* lse, float* tgt, float* nll,
+                               cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  dim3 block(kCombRows, kCombSlices);
+  dim3 grid((unsigned)ceil_div(N, kCombRows));
+  lse_combine_kernel<<<grid, block, 0, stream>>>(part_max, part_sum, part_tgt, P, N, ld, lse, tgt, nll);
+  return launched();
+}
+
+cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int32_t* targets,
+                              const float* d_nll, int64_t N, int64_t V, int64_t v_offset,
+                              float log_eps, bool no_filter, uint8_t* keep, int64_t* skip_stats,
+                              cudaStream_t stream) {
+  if (N == 0 || V == 0) return cudaSuccess;
+  dim3 grid((unsigned)ceil_div(V, kStatTile), (unsigned)ceil_div(N, kRowBlock));
+  block_mask_kernel<<<grid, kRowBlock, 0, stream>>>(tile_max, lse, targets, d_nll, N, V, v_offset,
+                                                    log_eps, no_filter ? 1 : 0, keep,
+                                                    reinterpret_cast<unsigned long long*>(skip_stats));
+  return launched();
+}
+
+cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const int grid = grid_for(n, threads);
+  switch (dtype) {
+    case CCE_F32:
+      return cudaMemcpyAsync(dst, src, n * sizeof(float), cudaMemcpyDeviceToDevice, stream);
+    case CCE_F16:
+      cast_f32_kernel<__half><<<grid, threads, 0, stream>>>(src, (__half*)dst, n);
+      break;
+    case CCE_BF16:
+      cast_f32_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(src, (__nv_bfloat16*)dst, n);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return launched();
+}
+
+cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  fill_f32_kernel<<<grid_for(n, 256), 256, 0, stream>>>(dst, v, n);
+  return launched();
+}
+
+}  // namespace cce

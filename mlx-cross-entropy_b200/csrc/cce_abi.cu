@@ -1,0 +1,264 @@
+// C-ABI layer: argument validation, workspace carving and kernel dispatch.
+//
+// Mirrors the host side of the reference's op layer: shape / dtype checks of
+// csrc/cce/cce.cpp:41-73 (returned as status codes instead of thrown
+// exceptions), output and zero-fill set-up of cce.cpp:243-246 and :316-340,
+// and the dtype-keyed kernel choice of cce.cpp:221-231, :300-310.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace cce {
+
+std::atomic<uint64_t> g_launches{0};
+
+cudaError_t launched() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+}  // namespace cce
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* where) {
+  return fail(CCE_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)err, cudaGetErrorString(err));
+}
+
+#define CCE_CUDA_CHECK(expr, where)          \
+  do {                                       \
+    cudaError_t _e = (expr);                 \
+    if (_e != cudaSuccess) return cuda_fail(_e, where); \
+  } while (0)
+
+constexpr size_t kAlign = 256;
+constexpr int64_t kDlBudgetBytes = 128ll << 20;  // dlogits chunk buffer budget
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool dtype_ok(int d) { return d == CCE_F32 || d == CCE_F16 || d == CCE_BF16; }
+size_t dtype_size(int d) { return d == CCE_F32 ? 4 : 2; }
+
+std::atomic<int> g_arch[64];
+
+int check_arch() {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return CCE_OK;
+  int cc = g_arch[dev].load(std::memory_order_relaxed);
+  if (cc == 0) {
+    int major = 0, minor = 0;
+    err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute");
+    err = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute");
+    cc = major * 10 + minor;
+    g_arch[dev].store(cc, std::memory_order_relaxed);
+  }
+  if (cc != 100)
+    return fail(CCE_ERR_ARCH, "device %d has compute capability %d.%d; this library is built for sm_100a (B200)",
+                dev, cc / 10, cc % 10);
+  return CCE_OK;
+}
+
+// Vocabulary rows per backward chunk and whether the tensor-core path runs.
+struct BwdPlan {
+  bool tc;
+  int64_t vc;        // chunk rows (also the dlogits row stride)
+  size_t keep_bytes, dl_bytes, acc_bytes;
+};
+
+bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
+
+BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {
+  BwdPlan p{};
+  p.tc = tc;
+  const int64_t gran = tc ? 256 : 128;
+  const int64_t elt = tc ? 2 : 4;
+  const int64_t nrow = N > 0 ? N : 1;
+  int64_t vc = (kDlBudgetBytes / (nrow * elt)) / gran * gran;
+  if (vc < gran) vc = gran;
+  const int64_t vmax = cce::round_up(V > 0 ? V : 1, gran);
+  if (vc > vmax) vc = vmax;
+  p.vc = vc;
+  p.keep_bytes = align_up((size_t)cce::ceil_div(N, cce::kRowBlock) * (size_t)cce::ceil_div(V, cce::kStatTile));
+  p.dl_bytes = align_up((size_t)N * (size_t)vc * (size_t)elt);
+  p.acc_bytes = ((flags & CCE_NEED_DE) && !(flags & CCE_DE_F32)) ? align_up((size_t)N * (size_t)D * 4) : 0;
+  return p;
+}
+
+size_t plan_bytes(const BwdPlan& p) { return p.keep_bytes + p.dl_bytes + p.acc_bytes; }
+
+int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
+  if (N < 0 || D <= 0 || V < 0) return fail(CCE_ERR_SHAPE, "bad sizes N=%lld D=%lld V=%lld", (long long)N, (long long)D, (long long)V);
+  if (N > (1ll << 31) || V > (1ll << 31) || D > (1ll << 20))
+    return fail(CCE_ERR_SHAPE, "sizes out of supported range N=%lld D=%lld V=%lld", (long long)N, (long long)D, (long long)V);
+  if (!dtype_ok(dtype)) return fail(CCE_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  return CCE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cce_version(void) { return 100; }
+
+const char* cce_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t cce_launch_count(void) { return cce::g_launches.load(std::memory_order_relaxed); }
+
+int64_t cce_num_stat_tiles(int64_t V) { return V <= 0 ? 0 : cce::ceil_div(V, cce::kStatTile); }
+
+size_t cce_forward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
+  (void)D;
+  (void)dtype;
+  return align_up((size_t)cce_num_stat_tiles(V) * (size_t)(N > 0 ? N : 0) * sizeof(float));
+}
+
+int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
+                const int32_t* targets, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                int dtype, float* tile_max, float* lse, float* tgt, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  int rc = check_sizes(N, D, V, dtype);
+  if (rc) return rc;
+  if (bias && !dtype_ok(bias_dtype)) return fail(CCE_ERR_DTYPE, "unsupported bias dtype code %d", bias_dtype);
+  if (N == 0) return CCE_OK;
+  if (V == 0) return fail(CCE_ERR_SHAPE, "V must be positive");
+  if (!e || !c || !targets || !tile_max || !lse || !tgt)
+    return fail(CCE_ERR_ARG, "cce_forward: NULL required pointer");
+  const size_t need = cce_forward_workspace_bytes(N, D, V, dtype);
+  if (!workspace || workspace_bytes < need)
+    return fail(CCE_ERR_WORKSPACE, "cce_forward: workspace %zu bytes < required %zu", workspace_bytes, need);
+  rc = check_arch();
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  cce::FwdArgs a{e, c, bias, bias_dtype, targets, N, D, V, v_offset, dtype, tile_max,
+                 (float*)workspace, tgt};
+  // Rows whose target is not in this call's vocabulary range keep tgt = 0.
+  CCE_CUDA_CHECK(cudaMemsetAsync(tgt, 0, (size_t)N * sizeof(float), s), "cce_forward memset");
+  if (cce::tc_supported(e, c, D, dtype)) {
+    CCE_CUDA_CHECK(cce::tc_forward(a, s), "cce_forward tc kernel");
+  } else {
+    CCE_CUDA_CHECK(cce::simt_forward(a, s), "cce_forward simt kernel");
+  }
+  CCE_CUDA_CHECK(cce::launch_lse_combine(tile_max, (const float*)workspace, nullptr,
+                                         cce_num_stat_tiles(V), N, N, lse, nullptr, nullptr, s),
+                 "cce_forward combine");
+  return CCE_OK;
+}
+
+int cce_lse_combine(const float* part_lse, const float* part_tgt, int64_t P, int64_t N,
+                    int64_t part_stride, float* lse, float* tgt, float* nll, void* stream) {
+  if (P <= 0 || N < 0) return fail(CCE_ERR_SHAPE, "cce_lse_combine: bad P=%lld N=%lld", (long long)P, (long long)N);
+  if (P > 1 && part_stride < N)
+    return fail(CCE_ERR_SHAPE, "cce_lse_combine: part_stride %lld < N %lld", (long long)part_stride, (long long)N);
+  if (N == 0) return CCE_OK;
+  if (!part_lse || !lse) return fail(CCE_ERR_ARG, "cce_lse_combine: NULL required pointer");
+  if (tgt && !part_tgt) return fail(CCE_ERR_ARG, "cce_lse_combine: tgt requested without part_tgt");
+  if (nll && !part_tgt) return fail(CCE_ERR_ARG, "cce_lse_combine: nll requested without part_tgt");
+  int rc = check_arch();
+  if (rc) return rc;
+  CCE_CUDA_CHECK(cce::launch_lse_combine(part_lse, nullptr, part_tgt, P, N, part_stride, lse, tgt,
+                                         nll, (cudaStream_t)stream),
+                 "cce_lse_combine");
+  return CCE_OK;
+}
+
+size_t cce_backward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags) {
+  size_t b = plan_bytes(plan_backward(N, D, V, dtype, flags, false));
+  if (tc_candidate(dtype, D)) {
+    const size_t t = plan_bytes(plan_backward(N, D, V, dtype, flags, true));
+    if (t > b) b = t;
+  }
+  return b;
+}
+
+int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
+                 const int32_t* targets, const float* lse, const float* d_nll,
+                 const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                 int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
+                 float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  int rc = check_sizes(N, D, V, dtype);
+  if (rc) return rc;
+  if (bias && !dtype_ok(bias_dtype)) return fail(CCE_ERR_DTYPE, "unsupported bias dtype code %d", bias_dtype);
+  if (flags & ~(CCE_NEED_DE | CCE_NEED_DC | CCE_NEED_DBIAS | CCE_DE_F32 | CCE_NO_FILTER))
+    return fail(CCE_ERR_ARG, "cce_backward: unknown flag bits 0x%x", flags);
+  const bool need_de = flags & CCE_NEED_DE, need_dc = flags & CCE_NEED_DC,
+             need_db = flags & CCE_NEED_DBIAS;
+  if ((need_de && !grad_e) || (need_dc && !grad_c) || (need_db && !grad_bias))
+    return fail(CCE_ERR_ARG, "cce_backward: a requested gradient has a NULL output pointer");
+  if (need_db && !bias) return fail(CCE_ERR_ARG, "cce_backward: CCE_NEED_DBIAS without bias");
+  if (!need_de && !need_dc && !need_db) return CCE_OK;
+  if (V == 0) return fail(CCE_ERR_SHAPE, "V must be positive");
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = check_arch();
+  if (rc) return rc;
+  if (N == 0) {
+    // No rows: every requested gradient is zero.
+    if (need_dc) CCE_CUDA_CHECK(cudaMemsetAsync(grad_c, 0, (size_t)V * D * dtype_size(dtype), s), "memset grad_c");
+    if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
+    return CCE_OK;
+  }
+  if (!e || !c || !targets || !lse || !d_nll || !tile_max)
+    return fail(CCE_ERR_ARG, "cce_backward: NULL required pointer");
+  const bool tc = cce::tc_supported(e, c, D, dtype) && cce::tc_supported(grad_c ? grad_c : c, e, D, dtype);
+  const BwdPlan p = plan_backward(N, D, V, dtype, flags, tc);
+  const size_t need = cce_backward_workspace_bytes(N, D, V, dtype, flags);
+  if (!workspace || workspace_bytes < need)
+    return fail(CCE_ERR_WORKSPACE, "cce_backward: workspace %zu bytes < required %zu", workspace_bytes, need);
+
+  char* ws = (char*)workspace;
+  uint8_t* keep = (uint8_t*)ws;
+  void* dl = ws + p.keep_bytes;
+  float* acc = nullptr;
+  if (need_de) acc = (flags & CCE_DE_F32) ? (float*)grad_e : (float*)(ws + p.keep_bytes + p.dl_bytes);
+
+  CCE_CUDA_CHECK(cce::launch_block_mask(tile_max, lse, targets, d_nll, N, V, v_offset, filter_log_eps,
+                                        (flags & CCE_NO_FILTER) != 0, keep, skip_stats, s),
+                 "cce_backward mask");
+  if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
+
+  cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, N, D, V, v_offset, dtype,
+                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr};
+  const int64_t nchunks = cce::ceil_div(V, p.vc);
+  for (int64_t ch = 0; ch < nchunks; ++ch) {
+    a.vc0 = ch * p.vc;
+    a.vc_len = (V - a.vc0) < p.vc ? (V - a.vc0) : p.vc;
+    const bool last = ch == nchunks - 1;
+    if (p.tc) {
+      CCE_CUDA_CHECK(cce::tc_dlogits(a, s), "cce_backward tc dlogits");
+      if (need_de) {
+        const bool write_out = last && !(flags & CCE_DE_F32);
+        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, write_out ? grad_e : nullptr, write_out, s),
+                       "cce_backward tc grad_e");
+      }
+      if (need_dc) CCE_CUDA_CHECK(cce::tc_grad_c(a, grad_c, s), "cce_backward tc grad_c");
+    } else {
+      CCE_CUDA_CHECK(cce::simt_dlogits(a, s), "cce_backward simt dlogits");
+      if (need_de) CCE_CUDA_CHECK(cce::simt_grad_e(a, acc, ch > 0, s), "cce_backward simt grad_e");
+      if (need_dc) CCE_CUDA_CHECK(cce::simt_grad_c(a, grad_c, s), "cce_backward simt grad_c");
+      if (need_de && last && !(flags & CCE_DE_F32))
+        CCE_CUDA_CHECK(cce::launch_cast_f32(acc, grad_e, dtype, N * D, s), "cce_backward cast grad_e");
+    }
+  }
+  return CCE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+// Internal launch interface between the C-ABI layer (cce_abi.cu) and the
+// kernel translation units.  All launchers enqueue on `stream` and return the
+// cudaError_t of the launch.
+#pragma once
+
+#include "common.cuh"
+
+namespace cce {
+
+// Counts one kernel launch (cce_launch_count) and returns cudaGetLastError().
+cudaError_t launched();
+
+struct FwdArgs {
+  const void* e;
+  const void* c;
+  const void* bias;
+  int bias_dtype;
+  const int32_t* targets;
+  int64_t N, D, V, v_offset;
+  int dtype;
+  float* tile_max;  // [nVt][N]
+  float* tile_sum;  // [nVt][N] (workspace)
+  float* tgt;       // [N]
+};
+
+struct BwdChunkArgs {
+  const void* e;
+  const void* c;
+  const void* bias;
+  int bias_dtype;
+  const int32_t* targets;
+  const float* lse;
+  const float* d_nll;
+  const uint8_t* keep;   // [nRb][nVt] block mask
+  int64_t N, D, V, v_offset;
+  int dtype;
+  int64_t vc0;           // first local vocab row of the chunk
+  int64_t vc_len;        // rows in the chunk
+  int64_t vc_ld;         // row stride of the dlogits buffer (elements)
+  void* dlogits;         // [N][vc_ld], fp32 (SIMT path) or 16-bit (tensor-core path)
+  float* grad_bias;      // [V] fp32 or nullptr
+};
+
+// ---- auxiliary kernels (aux_kernels.cu) ----
+// (max, sum-exp) pairs, row p at part_max + p * ld (part_sum == nullptr: the
+// entries are LSEs, i.e. pairs with sum 1)
+cudaError_t launch_lse_combine(const float* part_max, const float* part_sum, const float* part_tgt,
+                               int64_t P, int64_t N, int64_t ld, float* lse, float* tgt, float* nll,
+                               cudaStream_t stream);
+cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int32_t* targets,
+                              const float* d_nll, int64_t N, int64_t V, int64_t v_offset,
+                              float log_eps, bool no_filter, uint8_t* keep, int64_t* skip_stats,
+                              cudaStream_t stream);
+cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, cudaStream_t stream);
+cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t stream);
+
+// ---- SIMT kernels (simt_kernels.cu): any dtype, any shape ----
+cudaError_t simt_forward(const FwdArgs& a, cudaStream_t stream);
+cudaError_t simt_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
+// grad_e_acc[N, D] (+)= dl[N, vc_len] @ c[v_offset-local rows vc0.., D]
+cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, cudaStream_t stream);
+// grad_c[vc0 .. vc0+vc_len, D] = dl^T @ e, written in dtype
+cudaError_t simt_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
+
+// ---- tcgen05 kernels (tc_kernels.cu): 16-bit dtypes, D % 8 == 0 ----
+bool tc_supported(const void* e, const void* c, int64_t D, int dtype);
+cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
+cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
+                      bool write_out, cudaStream_t stream);
+cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
+
+}  // namespace cce

@@ -1,0 +1,109 @@
+"""CPU tests of the C-ABI library and the host-side API logic (no kernel runs)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import mlx_cce
+from mlx_cce import _ext
+from mlx_cce._autograd import sanitize_targets
+from mlx_cce.distributed import vocab_shard
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _header_symbols():
+    text = "\n".join(p.read_text() for p in (REPO / "include").glob("*.h"))
+    return set(re.findall(r"CCE_API\s+[\w\s\*]+?\b(cce_\w+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol():
+    declared = _header_symbols()
+    assert declared, "no CCE_API declarations found in include/*.h"
+    lib = ctypes.CDLL(str(_ext._LIB_PATH))
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert set(_ext.EXPORTED_SYMBOLS) == declared
+
+
+def test_version_and_tile_count():
+    assert _ext.version() == 100
+    assert _ext.num_stat_tiles(128256) == 1002
+    assert _ext.num_stat_tiles(128) == 1
+    assert _ext.num_stat_tiles(129) == 2
+    assert _ext.num_stat_tiles(0) == 0
+
+
+def test_workspace_sizes():
+    lib = _ext.lib
+    f = lib.cce_forward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16)
+    assert f >= 1002 * 4096 * 4 and f % 256 == 0
+    flags = _ext.CCE_NEED_DE | _ext.CCE_NEED_DC
+    b = lib.cce_backward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16, flags)
+    # mask + a bounded dlogits chunk (never [N, V]) + the fp32 grad_e accumulator
+    assert b < 4096 * 128256 * 2
+    assert b >= 4096 * 4096 * 4
+    b32 = lib.cce_backward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16,
+                                           flags | _ext.CCE_DE_F32)
+    assert b32 < b
+
+
+def test_error_codes_without_gpu_work():
+    lib = _ext.lib
+    # bad dtype / sizes are rejected before any CUDA call
+    rc = lib.cce_forward(None, None, None, 0, None, 4, 8, 16, 0, 7, None, None, None, None, 0, None)
+    assert rc == _ext.CCE_ERR_DTYPE
+    assert b"dtype" in lib.cce_last_error()
+    rc = lib.cce_forward(None, None, None, 0, None, -1, 8, 16, 0, 0, None, None, None, None, 0, None)
+    assert rc == _ext.CCE_ERR_SHAPE
+    rc = lib.cce_backward(None, None, None, 0, None, None, None, None, 4, 8, 16, 0, 0, 1 << 9,
+                          -8.0, None, None, None, None, None, 0, None)
+    assert rc == _ext.CCE_ERR_ARG
+    rc = lib.cce_backward(None, None, None, 0, None, None, None, None, 4, 8, 16, 0, 0,
+                          _ext.CCE_NEED_DE, -8.0, None, None, None, None, None, 0, None)
+    assert rc == _ext.CCE_ERR_ARG
+    rc = lib.cce_lse_combine(None, None, 0, 4, 4, None, None, None, None)
+    assert rc == _ext.CCE_ERR_SHAPE
+
+
+def test_python_api_rejects_cpu_tensors_and_bad_args():
+    e = torch.randn(8, 16)
+    c = torch.randn(32, 16)
+    t = torch.randint(0, 32, (8,))
+    with pytest.raises(ValueError, match="Unknown reduction"):
+        mlx_cce.linear_cross_entropy(e, c, t, reduction="avg")
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        mlx_cce.linear_cross_entropy(e, c, t)
+    with pytest.raises(ValueError, match="2D"):
+        mlx_cce.cce_loss(e[None], c, t)
+    with pytest.raises(ValueError):
+        _ext.forward(e, c[:, :8], t.to(torch.int32))
+    with pytest.raises(ValueError, match="int32"):
+        _ext.forward(e, c, t)
+    with pytest.raises(ValueError, match="share a dtype"):
+        _ext.forward(e, c.half(), t.to(torch.int32))
+    with pytest.raises(ValueError, match="unsupported dtype"):
+        _ext.dtype_code(torch.float64, "x")
+
+
+def test_sanitize_targets():
+    t = torch.tensor([[3, -100, 7], [-100, 0, 5]])
+    safe, valid = sanitize_targets(t, -100)
+    assert safe.dtype == torch.int32
+    assert safe.tolist() == [3, 0, 7, 0, 0, 5]
+    assert valid.tolist() == [True, False, True, False, True, True]
+    safe, valid = sanitize_targets(torch.tensor([1, 2]), None)
+    assert valid.all() and safe.tolist() == [1, 2]
+
+
+@pytest.mark.parametrize("V,world", [(128256, 8), (128256, 3), (10, 4), (7, 8)])
+def test_vocab_shard_partition(V, world):
+    spans = [vocab_shard(V, r, world) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == V
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 == b0 and a1 >= a0
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1

@@ -1,0 +1,305 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Tolerances (BASELINE): loss relative 1e-3 for 16-bit inputs with fp32
+accumulation and 1e-5 for fp32 inputs; gradients relative max-abs
+(max |got - ref| / max |ref|) 2e-2.  The oracle is float64.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import mlx_cce
+from mlx_cce import _ext, synthetic
+from mlx_cce.distributed import vocab_shard
+from oracle import cce_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+LOSS_RTOL = {torch.float32: 1e-5, torch.float16: 1e-3, torch.bfloat16: 1e-3}
+GRAD_TOL = 2e-2
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+def run(e, c, t, bias=None, reduction="mean", ignore_index=-100, grad_out=None, need_c=True,
+        need_bias=None, **kw):
+    """Forward + backward through the public API on cuda:0; returns numpy float64."""
+    dev = _dev()
+    e_ = e.to(dev).requires_grad_(True)
+    c_ = c.to(dev).requires_grad_(need_c)
+    b_ = None
+    if bias is not None:
+        b_ = bias.to(dev).requires_grad_(need_bias if need_bias is not None else True)
+    t_ = t.to(dev)
+    loss = mlx_cce.linear_cross_entropy(e_, c_, t_, bias=b_, reduction=reduction,
+                                        ignore_index=ignore_index, **kw)
+    if reduction == "none":
+        go = grad_out.to(dev) if grad_out is not None else torch.ones_like(loss)
+        loss.backward(go)
+    else:
+        loss.backward()
+    torch.cuda.synchronize()
+    f = lambda x: None if x is None else x.detach().double().cpu().numpy()
+    return dict(loss=f(loss), dE=f(e_.grad), dC=f(c_.grad) if need_c else None,
+                dB=f(b_.grad) if b_ is not None and b_.requires_grad else None)
+
+
+def oracle(e, c, t, bias=None, reduction="mean", ignore_index=-100, grad_out=None):
+    f = lambda x: None if x is None else x.double().numpy()
+    loss, lse, dE, dC, dB = O.loss_and_grads(
+        f(e.reshape(-1, e.shape[-1])), f(c), t.reshape(-1).numpy(), f(bias), reduction,
+        ignore_index, None if grad_out is None else grad_out.reshape(-1).double().numpy())
+    return dict(loss=loss, lse=lse, dE=dE, dC=dC, dB=dB)
+
+
+def check(got, ref, dtype, grads=("dE", "dC", "dB"), grad_tol=GRAD_TOL):
+    np.testing.assert_allclose(got["loss"].reshape(-1), np.asarray(ref["loss"]).reshape(-1),
+                               rtol=LOSS_RTOL[dtype], atol=1e-6)
+    for k in grads:
+        if ref.get(k) is None or got.get(k) is None:
+            continue
+        err = O.rel_max_abs(got[k].reshape(ref[k].shape), ref[k])
+        assert err < grad_tol, f"{k}: rel max-abs {err:.3e} >= {grad_tol}"
+
+
+def small(N, D, V, dtype, seed=0, c_std=None, bias=None, ignore=0.0):
+    g = torch.Generator().manual_seed(seed)
+    e = torch.randn(N, D, generator=g)
+    c = torch.randn(V, D, generator=g) * (c_std if c_std is not None else D ** -0.5)
+    t = torch.randint(0, V, (N,), generator=g)
+    if ignore:
+        t[torch.randperm(N, generator=g)[: int(round(ignore * N))]] = -100
+    b = None
+    if bias is not None:
+        b = (torch.randn(V, generator=g) * 0.5).to(bias)
+    return e.to(dtype), c.to(dtype), t, b
+
+
+DTYPES = [torch.float32, torch.bfloat16, torch.float16]
+
+
+# --- the reference's own test cases (tests/test_correctness.py, test_gradients.py) ---
+
+@pytest.mark.parametrize("B,D,V", [(32, 64, 1024), (64, 128, 4096), (128, 256, 32000),
+                                   (32, 2048, 128256)])
+@pytest.mark.parametrize("name,dtype", [("f32", torch.float32), ("bf16", torch.bfloat16)])
+def test_reference_shapes_golden(B, D, V, name, dtype):
+    import sys
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden as MG
+    fx = np.load(GOLDEN / f"ref_{B}x{D}x{V}_{name}.npz")
+    e, c, t = MG.ref_inputs(B, D, V, dtype=dtype)
+    got = run(e, c, t, return_lse=False)
+    np.testing.assert_allclose(got["loss"], fx["loss"], rtol=LOSS_RTOL[dtype])
+    rows, cols = fx["rows"], fx["cols"]
+    assert O.rel_max_abs(got["dE"][rows], fx["dE_rows"]) < GRAD_TOL
+    assert O.rel_max_abs(got["dC"][cols], fx["dC_cols"]) < GRAD_TOL
+
+
+@pytest.mark.parametrize("reduction", ["none", "sum", "mean"])
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_reductions(reduction, dtype):
+    e, c, t, _ = small(32, 64, 1024, dtype, seed=1, ignore=0.1)
+    go = torch.randn(32, generator=torch.Generator().manual_seed(2)) if reduction == "none" else None
+    check(run(e, c, t, reduction=reduction, grad_out=go),
+          oracle(e, c, t, reduction=reduction, grad_out=go), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_ignore_index_rows_have_zero_grad(dtype):
+    e, c, t, _ = small(32, 64, 1024, dtype, seed=3)
+    t[16:] = -100
+    got = run(e, c, t)
+    check(got, oracle(e, c, t), dtype)
+    assert np.all(got["dE"][16:] == 0.0)
+
+
+def test_ignore_index_none_and_custom():
+    e, c, t, _ = small(40, 64, 500, torch.bfloat16, seed=4)
+    check(run(e, c, t, ignore_index=None), oracle(e, c, t, ignore_index=None), torch.bfloat16)
+    t2 = t.clone()
+    t2[::3] = 7
+    check(run(e, c, t2, ignore_index=7), oracle(e, c, t2, ignore_index=7), torch.bfloat16)
+
+
+def test_all_rows_ignored():
+    e, c, t, _ = small(64, 32, 300, torch.bfloat16, seed=5)
+    t[:] = -100
+    got = run(e, c, t)
+    assert got["loss"] == 0.0
+    assert np.all(got["dE"] == 0) and np.all(got["dC"] == 0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("bias_dtype", [torch.float32, "same"])
+def test_bias(dtype, bias_dtype):
+    bdt = dtype if bias_dtype == "same" else bias_dtype
+    e, c, t, b = small(48, 64, 1000, dtype, seed=6, bias=bdt)
+    check(run(e, c, t, bias=b), oracle(e, c, t, bias=b), dtype)
+
+
+def test_batched_sequence():
+    g = torch.Generator().manual_seed(42)
+    B, T, D, V = 4, 128, 256, 4096
+    e = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    c = (torch.randn(V, D, generator=g) * 0.05).to(torch.bfloat16)
+    t = torch.randint(0, V, (B, T), generator=g)
+    got = run(e, c, t, reduction="none")
+    assert got["loss"].shape == (B, T)
+    ref = oracle(e, c, t, reduction="none")
+    check(got, ref, torch.bfloat16)
+
+
+def test_cut_cross_entropy_matches_cce_loss():
+    e, c, t, _ = small(32, 64, 1024, torch.float32, seed=7)
+    dev = _dev()
+    a = mlx_cce.cut_cross_entropy(e.to(dev), c.to(dev), t.to(dev))
+    b = mlx_cce.cce_loss(e.to(dev), c.to(dev), t.to(dev))
+    np.testing.assert_allclose(a.item(), b.item(), rtol=1e-5)
+
+
+def test_raw_entry_points():
+    e, c, t, _ = small(64, 64, 700, torch.bfloat16, seed=8)
+    dev = _dev()
+    ed, cd, td = e.to(dev), c.to(dev), t.to(dev)
+    tm, ts, neg_tgt, lse = mlx_cce.cce_forward_raw(ed, cd, td)
+    ref = oracle(e, c, t)
+    np.testing.assert_allclose(lse.double().cpu().numpy(), ref["lse"], rtol=1e-3)
+    assert tm.numel() == _ext.num_stat_tiles(700) * 64
+    nll = (lse + neg_tgt).double().cpu().numpy()
+    np.testing.assert_allclose(nll.mean(), ref["loss"], rtol=1e-3)
+    d_nll = torch.full((64,), 1.0 / 64, device=dev)
+    dE = mlx_cce.cce_backward_raw(ed, cd, lse, td, d_nll, tm)
+    assert dE.dtype == torch.bfloat16
+    assert O.rel_max_abs(dE.double().cpu().numpy(), ref["dE"]) < GRAD_TOL
+    dE2, dC2, dB2 = mlx_cce.cce_backward_raw(ed, cd, lse, td, d_nll, tm, compute_all_grads=True)
+    assert O.rel_max_abs(dC2.double().cpu().numpy(), ref["dC"]) < GRAD_TOL
+
+
+# --- edge cases: ragged sizes, tiny sizes, unaligned D ---
+
+@pytest.mark.parametrize("N,D,V", [(1, 64, 1000), (33, 64, 129), (130, 72, 1000), (257, 128, 4097),
+                                   (64, 8, 300), (64, 100, 513), (5, 16, 1), (128, 64, 16032 + 32)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ragged_shapes(N, D, V, dtype):
+    e, c, t, _ = small(N, D, V, dtype, seed=N + D + V, ignore=0.1 if N > 10 else 0.0)
+    if N > 2:
+        t[0] = V - 1
+        t[1] = 0
+    check(run(e, c, t), oracle(e, c, t), dtype)
+
+
+def test_empty_batch():
+    dev = _dev()
+    e = torch.zeros(0, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    c = torch.randn(100, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    t = torch.zeros(0, dtype=torch.int64, device=dev)
+    loss = mlx_cce.linear_cross_entropy(e, c, t)
+    loss.backward()
+    assert loss.item() == 0.0
+    assert torch.all(c.grad == 0)
+
+
+def test_non_default_stream():
+    e, c, t, _ = small(64, 64, 1000, torch.bfloat16, seed=9)
+    dev = _dev()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        got = run(e, c, t)
+    torch.cuda.synchronize()
+    check(got, oracle(e, c, t), torch.bfloat16)
+
+
+def test_no_filter_is_exact_and_filter_reports_skips():
+    e, c, t, _, _, _ = synthetic.make_inputs(3, N=256, V=8192, D=512)
+    dev = _dev()
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    got = run(e, c, t, skip_stats=stats)
+    ref = oracle(e, c, t)
+    check(got, ref, torch.bfloat16)
+    skipped, total = stats.tolist()
+    assert total == 2 * 64
+    got_exact = run(e, c, t, filter_log_eps=-float("inf"))
+    check(got_exact, ref, torch.bfloat16, grad_tol=1e-2)
+
+
+# --- vocabulary sharding, emulated on one GPU ---
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_vocab_sharded_composition(world):
+    e, c, t, b = small(96, 64, 2000, torch.bfloat16, seed=10, bias=torch.float32, ignore=0.1)
+    dev = _dev()
+    ed, cd, bd = e.to(dev), c.to(dev), b.to(dev)
+    safe, valid = mlx_cce._autograd.sanitize_targets(t.to(dev), -100)
+    parts, stats = [], []
+    for r in range(world):
+        v0, v1 = vocab_shard(2000, r, world)
+        tm, lse_r, tgt_r = _ext.forward(ed, cd[v0:v1].contiguous(), safe, bd[v0:v1].contiguous(),
+                                        v_offset=v0)
+        parts.append((v0, v1, tm))
+        stats.append(torch.stack([lse_r, tgt_r]))
+    g = torch.stack(stats)                         # [world, 2, N]
+    lse, tgt, nll = _ext.lse_combine(g[:, 0, :], g[:, 1, :])
+    ref = oracle(e, c, t, bias=b)
+    np.testing.assert_allclose(lse.double().cpu().numpy(), ref["lse"], rtol=1e-3)
+    loss = (nll * valid).sum() / valid.sum()
+    np.testing.assert_allclose(loss.item(), ref["loss"], rtol=1e-3)
+    d_nll = (valid.float() / valid.sum()).contiguous()
+    ge = torch.zeros(96, 64, dtype=torch.float32, device=dev)
+    gcs = []
+    for v0, v1, tm in parts:
+        ge_r, gc_r, gb_r = _ext.backward(ed, cd[v0:v1].contiguous(), safe, lse, d_nll, tm,
+                                         bd[v0:v1].contiguous(), v_offset=v0, need_c=True,
+                                         need_bias=True, grad_e_f32=True)
+        ge += ge_r
+        gcs.append(gc_r)
+    assert O.rel_max_abs(ge.double().cpu().numpy(), ref["dE"]) < GRAD_TOL
+    gc = torch.cat(gcs).double().cpu().numpy()
+    assert O.rel_max_abs(gc, ref["dC"]) < GRAD_TOL
+
+
+# --- BASELINE workloads against the golden fixtures ---
+
+def _cfg_check(cfg):
+    fx = np.load(GOLDEN / f"cfg{cfg}.npz")
+    e, c, t, bias, go, w = synthetic.make_inputs(cfg)
+    dev = _dev()
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    got = run(e, c, t, bias=bias, reduction=w.reduction, grad_out=go, skip_stats=stats)
+    if w.reduction == "none":
+        np.testing.assert_allclose(got["loss"].reshape(-1), fx["loss"], rtol=LOSS_RTOL[w.dtype],
+                                   atol=1e-3 * np.abs(fx["loss"]).max())
+    else:
+        np.testing.assert_allclose(got["loss"], fx["loss"], rtol=LOSS_RTOL[w.dtype])
+    rows, cols = fx["rows"], fx["cols"]
+    errs = {"dE": O.rel_max_abs(got["dE"].reshape(-1, w.D)[rows], fx["dE_rows"]),
+            "dC": O.rel_max_abs(got["dC"][cols], fx["dC_cols"])}
+    if bias is not None:
+        errs["dB"] = O.rel_max_abs(got["dB"][cols], fx["dB_cols"])
+    for k, v in errs.items():
+        assert v < GRAD_TOL, f"cfg{cfg} {k}: {v:.3e}"
+    return stats.tolist()
+
+
+@pytest.mark.parametrize("cfg", [1, 2, 4])
+def test_workload_golden(cfg):
+    _cfg_check(cfg)
+
+
+def test_workload3_golden_and_no_nv_allocation():
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    skipped, total = _cfg_check(3)
+    w = synthetic.WORKLOADS[3]
+    assert total > 0 and 0 <= skipped <= total
+    # peak stays far below one [N, V] bf16 logits matrix on top of the
+    # inputs + their gradients (e, c, grad_e, grad_c)
+    peak = torch.cuda.max_memory_allocated() - base
+    io = 2 * (w.N * w.D + w.V * w.D) * 2
+    assert peak - io < w.N * w.V * 2 * 0.5, (peak, io)
