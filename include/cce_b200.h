@@ -79,6 +79,13 @@ CCE_API const char* cce_last_error(void);
  * reference. */
 CCE_API uint64_t cce_launch_count(void);
 
+/* Synchronous health check of the current device: CCE_OK, or CCE_ERR_CUDA if
+ * a tensor-core kernel gave up on a pipeline wait after its time limit (it then
+ * returns instead of hanging; its outputs are invalid).  reset != 0 clears the
+ * recorded state.  No counterpart in the reference (Metal kernels there cannot
+ * time out). */
+CCE_API int cce_device_status(int reset);
+
 /* Number of vocabulary tile statistics per row: ceil(V / CCE_STAT_TILE). */
 CCE_API int64_t cce_num_stat_tiles(int64_t V);
 

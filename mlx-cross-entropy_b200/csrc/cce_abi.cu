@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "kernels.cuh"
@@ -84,7 +85,7 @@ struct BwdPlan {
   size_t keep_bytes, dl_bytes, acc_bytes;
 };
 
-bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
+bool tc_candidate(int dtype, int64_t D) { return dtype == CCE_BF16 && D % 8 == 0; }
 
 BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {
   BwdPlan p{};
@@ -105,6 +106,18 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
 
 size_t plan_bytes(const BwdPlan& p) { return p.keep_bytes + p.dl_bytes + p.acc_bytes; }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// CCE_FORCE_SIMT=1 in the environment routes every call to the CUDA-core
+// kernels (used by the tests to compare both kernel families).
+bool force_simt() {
+  static const bool v = [] {
+    const char* s = getenv("CCE_FORCE_SIMT");
+    return s != nullptr && s[0] == '1';
+  }();
+  return v;
+}
+
 int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
   if (N < 0 || D <= 0 || V < 0) return fail(CCE_ERR_SHAPE, "bad sizes N=%lld D=%lld V=%lld", (long long)N, (long long)D, (long long)V);
   if (N > (1ll << 31) || V > (1ll << 31) || D > (1ll << 20))
@@ -122,6 +135,14 @@ int cce_version(void) { return 100; }
 const char* cce_last_error(void) { return g_last_error.c_str(); }
 
 uint64_t cce_launch_count(void) { return cce::g_launches.load(std::memory_order_relaxed); }
+
+int cce_device_status(int reset) {
+  const int v = cce::tc_read_status(reset != 0);
+  if (v < 0) return fail(CCE_ERR_CUDA, "cce_device_status: could not read the device status word");
+  if (v > 0)
+    return fail(CCE_ERR_CUDA, "a tensor-core kernel abandoned a pipeline wait after its time limit (code %d)", v);
+  return CCE_OK;
+}
 
 int64_t cce_num_stat_tiles(int64_t V) { return V <= 0 ? 0 : cce::ceil_div(V, cce::kStatTile); }
 
@@ -152,7 +173,7 @@ int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
                  (float*)workspace, tgt};
   // Rows whose target is not in this call's vocabulary range keep tgt = 0.
   CCE_CUDA_CHECK(cudaMemsetAsync(tgt, 0, (size_t)N * sizeof(float), s), "cce_forward memset");
-  if (cce::tc_supported(e, c, D, dtype)) {
+  if (!force_simt() && cce::tc_supported(e, c, D, dtype)) {
     CCE_CUDA_CHECK(cce::tc_forward(a, s), "cce_forward tc kernel");
   } else {
     CCE_CUDA_CHECK(cce::simt_forward(a, s), "cce_forward simt kernel");
@@ -218,7 +239,8 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   }
   if (!e || !c || !targets || !lse || !d_nll || !tile_max)
     return fail(CCE_ERR_ARG, "cce_backward: NULL required pointer");
-  const bool tc = cce::tc_supported(e, c, D, dtype) && cce::tc_supported(grad_c ? grad_c : c, e, D, dtype);
+  const bool tc = !force_simt() && cce::tc_backward_supported(e, c, D, dtype) && aligned16(workspace) &&
+                  (!need_de || aligned16(grad_e)) && (!need_dc || aligned16(grad_c));
   const BwdPlan p = plan_backward(N, D, V, dtype, flags, tc);
   const size_t need = cce_backward_workspace_bytes(N, D, V, dtype, flags);
   if (!workspace || workspace_bytes < need)

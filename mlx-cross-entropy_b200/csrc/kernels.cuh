@@ -64,6 +64,10 @@ cudaError_t simt_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream
 
 // ---- tcgen05 kernels (tc_kernels.cu): 16-bit dtypes, D % 8 == 0 ----
 bool tc_supported(const void* e, const void* c, int64_t D, int dtype);
+bool tc_backward_supported(const void* e, const void* c, int64_t D, int dtype);
+// Reads (and optionally clears) the tensor-core kernels' device status word:
+// 0 = ok, > 0 = code of a bounded wait that timed out, -1 = read failed.
+int tc_read_status(bool reset);
 cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
 cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
 cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,

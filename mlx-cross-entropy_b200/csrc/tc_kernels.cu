@@ -1,10 +1,679 @@
-// tcgen05 kernels (placeholder until the tensor-core path lands).
+// tcgen05 / TMEM / TMA kernels for 16-bit inputs (the hot path).
+//
+// One persistent, warp-specialised GEMM engine drives four epilogues:
+//
+//   K1 forward : S = e @ c^T per (128-row, 256-column) tile; the epilogue keeps
+//                an online max / sum-exp per row over each 128-column half,
+//                picks the target logit and adds the bias.  Replaces the tile
+//                kernel of csrc/cce/cce.metal:19-135 (which does the same per
+//                32x32 tile on 8x8 simdgroup MMAs).
+//   K4 dlogits : the same S for one vocabulary chunk, then
+//                w = d_nll * (exp(S + b - lse) - [v == t]) stored as bf16
+//                (cce.metal:274-282), with blocks the filter rejects
+//                (cce.metal:190-204) never computed; grad_bias column sums.
+//   K5 grad_e  : grad_e[N, D] (+)= w[N, chunk] @ c[chunk, D]   (cce.metal:284-291)
+//   K6 grad_c  : grad_c[chunk, D] = w^T @ e                    (cce.metal:292-304,
+//                reference/_fused_backward.py:1549-1567)
+//
+// Engine: 192 threads, one CTA per SM, grid = min(#tiles, #SMs), static
+// round-robin tile schedule.  Warp 0 lane 0 issues TMA loads of the A and B
+// K-slices (64 elements = one 128-byte swizzle row) into a 4-stage ring; warp 1
+// lane 0 issues tcgen05.mma (M=128, N=256, K=16) into one of two 256-column
+// fp32 TMEM accumulators and commits stage / accumulator barriers; warps 2-5
+// read the accumulator with tcgen05.ld (one TMEM lane = one output row per
+// thread) and run the epilogue while the next tile's MMAs proceed.
+#include <cuda.h>
+
+#include <atomic>
+#include <type_traits>
+
 #include "kernels.cuh"
+#include "tc_ptx.cuh"
 
 namespace cce {
-bool tc_supported(const void*, const void*, int64_t, int) { return false; }
-cudaError_t tc_forward(const FwdArgs&, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t tc_dlogits(const BwdChunkArgs&, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t tc_grad_e(const BwdChunkArgs&, float*, bool, void*, bool, cudaStream_t) { return cudaErrorNotSupported; }
-cudaError_t tc_grad_c(const BwdChunkArgs&, void*, cudaStream_t) { return cudaErrorNotSupported; }
+namespace tc {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;   // 16 KB
+constexpr uint32_t B_BYTES = BN * BK * 2;   // 32 KB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + 256;
+
+struct Sched {
+  int num_m, num_n, num_kb;
+  int m_fast;  // consecutive tile ids walk M first (1) or N first (0)
+  __device__ __forceinline__ void coords(int tile, int& mb, int& nb) const {
+    if (m_fast) {
+      mb = tile % num_m;
+      nb = tile / num_m;
+    } else {
+      nb = tile % num_n;
+      mb = tile / num_n;
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// helpers for the epilogues
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float* v) {
+  // 8 16-bit values = one 16-byte store
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    T lo = from_f32<T>(v[2 * i]), hi = from_f32<T>(v[2 * i + 1]);
+    w[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
+           ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// 32 bias values for columns [col0, col0 + 32), zero past `limit`.
+template <typename TB>
+__device__ __forceinline__ void load_bias32(const void* bias, int64_t col0, int64_t limit, float (&b)[32]) {
+  const TB* p = reinterpret_cast<const TB*>(bias);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) b[j] = (col0 + j < limit) ? to_f32(__ldg(p + col0 + j)) : 0.f;
+}
+
+// Sum each of 32 per-lane values across the warp's 32 lanes; afterwards lane
+// j holds the total of value j (recursive-halving transpose-reduce, 31 shuffles).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int i = 0; i < w; ++i) {
+      const float send = upper ? v[i] : v[i + w];
+      const float keep = upper ? v[i + w] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  return v[0];
+}
+
+// ---------------------------------------------------------------------------
+// K1: forward tile statistics
+// ---------------------------------------------------------------------------
+
+template <typename TB>  // bias element type; void = no bias
+struct FwdEpi {
+  const int32_t* targets;
+  const void* bias;
+  float* tile_max;
+  float* tile_sum;
+  float* tgt;
+  int64_t N, V, v_offset;
+
+  struct State {
+    int64_t row, tl, col0;
+    float m, s;
+  };
+
+  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+
+  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+    st.row = (int64_t)mb * BM + r;
+    st.tl = st.row < N ? (int64_t)targets[st.row] - v_offset : -1;
+    st.col0 = (int64_t)nb * BN;
+    st.m = -INFINITY;
+    st.s = 0.f;
+  }
+
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+    const int64_t cb = st.col0 + c * 32;
+    float b[32];
+    if constexpr (!std::is_void<TB>::value) {
+      load_bias32<TB>(bias, cb, V, b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) b[j] = 0.f;
+    }
+    float mc = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] = (cb + j < V) ? v[j] + b[j] : -INFINITY;
+      mc = fmaxf(mc, v[j]);
+      if (cb + j == st.tl && cb + j < V) tgt[st.row] = v[j];
+    }
+    const float nm = fmaxf(st.m, mc);
+    if (nm != -INFINITY) {
+      const float nml = nm * kLog2e;
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc += exp2f(fmaf(v[j], kLog2e, -nml));
+      st.s = st.s * exp2f(fmaf(st.m, kLog2e, -nml)) + acc;
+      st.m = nm;
+    }
+    if ((c & 3) == 3) {
+      const int h = c >> 2;
+      if (st.row < N && st.col0 + h * 128 < V) {
+        const int64_t idx = ((st.col0 >> 7) + h) * N + st.row;
+        tile_max[idx] = st.m;
+        tile_sum[idx] = st.s;
+      }
+      st.m = -INFINITY;
+      st.s = 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void end(State&) const {}
+};
+
+// ---------------------------------------------------------------------------
+// K4: dlogits of one vocabulary chunk
+// ---------------------------------------------------------------------------
+
+template <typename T, typename TB>
+struct DlogitsEpi {
+  const int32_t* targets;
+  const float* lse;
+  const float* d_nll;
+  const void* bias;
+  const uint8_t* keep;  // [nRb][nVt]
+  T* dl;                // [N][ld], column 0 = local vocab row vc0
+  float* grad_bias;     // [V] or nullptr
+  int64_t N, V, v_offset, vc0, vc_end, ld, nVt;
+
+  struct State {
+    int64_t row, tl, col0;
+    float g, L;
+    bool k0, k1;
+  };
+
+  __device__ __forceinline__ bool tile_active(int mb, int nb) const {
+    const int64_t t0 = (vc0 + (int64_t)nb * BN) >> 7;
+    const uint8_t* kr = keep + (int64_t)mb * nVt;
+    return kr[t0] || (t0 + 1 < nVt && kr[t0 + 1]);
+  }
+
+  __device__ __forceinline__ void inactive_tile(int mb, int nb, int r) const {
+    const int64_t row = (int64_t)mb * BM + r;
+    if (row >= N) return;
+    uint4* p = reinterpret_cast<uint4*>(dl + row * ld + (int64_t)nb * BN);
+#pragma unroll 4
+    for (int i = 0; i < BN * 2 / 16; ++i) p[i] = make_uint4(0, 0, 0, 0);
+  }
+
+  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+    st.row = (int64_t)mb * BM + r;
+    st.col0 = vc0 + (int64_t)nb * BN;  // local vocab id of the tile's column 0
+    const bool ok = st.row < N;
+    st.g = ok ? d_nll[st.row] : 0.f;
+    st.L = ok ? lse[st.row] : 0.f;
+    st.tl = ok ? (int64_t)targets[st.row] - v_offset : -1;
+    const int64_t t0 = st.col0 >> 7;
+    const uint8_t* kr = keep + (int64_t)mb * nVt;
+    st.k0 = kr[t0] != 0;
+    st.k1 = (t0 + 1 < nVt) && kr[t0 + 1] != 0;
+  }
+
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+    const int64_t cb = st.col0 + c * 32;
+    const bool kept = (c < 4) ? st.k0 : st.k1;
+    float b[32];
+    if constexpr (!std::is_void<TB>::value) {
+      load_bias32<TB>(bias, cb, vc_end, b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) b[j] = 0.f;
+    }
+    const float Ll = st.L * kLog2e;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float w = 0.f;
+      if (kept && cb + j < vc_end) {
+        w = st.g * exp2f(fmaf(v[j] + b[j], kLog2e, -Ll));
+        if (cb + j == st.tl) w -= st.g;
+      }
+      v[j] = w;
+    }
+    if (st.row < N) {
+      T* dst = dl + st.row * ld + (cb - vc0);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) store8<T>(dst + g * 8, v + g * 8);
+    }
+    if (grad_bias != nullptr) {
+      const int lane = threadIdx.x & 31;
+      const float colsum = warp_transpose_sum32(v);
+      if (kept && cb + lane < vc_end && colsum != 0.f) atomicAdd(grad_bias + cb + lane, colsum);
+    }
+  }
+
+  __device__ __forceinline__ void end(State&) const {}
+};
+
+// ---------------------------------------------------------------------------
+// K5: grad_e accumulation
+// ---------------------------------------------------------------------------
+
+template <typename T>
+struct GradEEpi {
+  float* acc;   // [N, D] fp32 accumulator
+  T* out;       // [N, D] final output (write_out)
+  int64_t N, D;
+  int accumulate, write_out;
+
+  struct State {
+    int64_t row, col0;
+  };
+  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+    st.row = (int64_t)mb * BM + r;
+    st.col0 = (int64_t)nb * BN;
+  }
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+    if (st.row >= N) return;
+    const int64_t cb = st.col0 + c * 32;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int64_t col = cb + g * 8;
+      if (col >= D) break;
+      float* a = acc + st.row * D + col;
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i];
+      if (accumulate) {
+        const float4 x0 = *reinterpret_cast<const float4*>(a);
+        const float4 x1 = *reinterpret_cast<const float4*>(a + 4);
+        o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
+        o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
+      }
+      if (write_out) {
+        store8<T>(out + st.row * D + col, o);
+      } else {
+        *reinterpret_cast<float4*>(a) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(a + 4) = make_float4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  }
+  __device__ __forceinline__ void end(State&) const {}
+};
+
+// ---------------------------------------------------------------------------
+// K6: grad_c store
+// ---------------------------------------------------------------------------
+
+template <typename T>
+struct GradCEpi {
+  T* out;        // grad_c + vc0 * D
+  int64_t rows, D;
+
+  struct State {
+    int64_t row, col0;
+  };
+  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+    st.row = (int64_t)mb * BM + r;
+    st.col0 = (int64_t)nb * BN;
+  }
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+    if (st.row >= rows) return;
+    const int64_t cb = st.col0 + c * 32;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int64_t col = cb + g * 8;
+      if (col >= D) break;
+      store8<T>(out + st.row * D + col, v + g * 8);
+    }
+  }
+  __device__ __forceinline__ void end(State&) const {}
+};
+
+// ---------------------------------------------------------------------------
+// the engine
+// ---------------------------------------------------------------------------
+
+template <bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const Sched sched, const Epi epi, const uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = sched.num_m * sched.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 128);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        sched.coords(tile, mb, nb);
+        if (!epi.tile_active(mb, nb)) continue;
+        bool ok = true;
+        for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
+          uint8_t* a = sA + stage * A_BYTES;
+          uint8_t* b = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_2d(a, &tmA, full + stage, mb * BM, k0);
+            tma_load_2d(a + BOX_MN_BYTES, &tmA, full + stage, mb * BM + 64, k0);
+          } else {
+            tma_load_2d(a, &tmA, full + stage, k0, mb * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
+          } else {
+            tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        sched.coords(tile, mb, nb);
+        if (!epi.tile_active(mb, nb)) continue;
+        if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = a_base + stage * A_BYTES;
+          const uint32_t b_addr = b_base + stage * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, BOX_MN_BYTES, 1024)
+                                     : smem_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, BOX_MN_BYTES, 1024)
+                                     : smem_desc(b_addr + k * 32, 16, 1024);
+            mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(empty + stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(tfull + acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      sched.coords(tile, mb, nb);
+      if (!epi.tile_active(mb, nb)) {
+        epi.inactive_tile(mb, nb, r);
+        continue;
+      }
+      if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
+      tc_fence_after();
+      typename Epi::State st;
+      epi.begin(st, mb, nb, r);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tbase + c * 32, v);
+        epi.chunk(st, c, v);
+      }
+      epi.end(st);
+      __syncwarp();
+      tc_fence_before();
+      mbar_arrive(tempty + acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+int num_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// Row-major [outer][inner] 16-bit matrix with row stride `ld` elements, read in
+// (box_inner x box_outer) boxes with 128-byte swizzling and zero fill.
+bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int64_t outer, int64_t ld,
+               uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool A_MN, bool B_MN, class Epi>
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sched& s, const Epi& epi,
+                        bool bf16, cudaStream_t stream) {
+  auto kern = tc_gemm_kernel<A_MN, B_MN, Epi>;
+  static std::atomic<int> attr_done[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    if (err != cudaSuccess) return err;
+    if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
+  }
+  const int tiles = s.num_m * s.num_n;
+  if (tiles == 0) return cudaSuccess;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, s, epi, idesc);
+  return launched();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace tc
+
+using namespace tc;
+
+bool tc_supported(const void* e, const void* c, int64_t D, int dtype) {
+  return (dtype == CCE_BF16 || dtype == CCE_F16) && D % 8 == 0 && aligned16(e) && aligned16(c) &&
+         encode_fn() != nullptr;
+}
+
+bool tc_backward_supported(const void* e, const void* c, int64_t D, int dtype) {
+  // fp16 dlogits would underflow (softmax * d_nll below 2^-24): bf16 only.
+  return dtype == CCE_BF16 && tc_supported(e, c, D, dtype);
+}
+
+namespace {
+
+template <typename TB>
+cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
+  const bool bf16 = a.dtype == CCE_BF16;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1};
+  FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
+  return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
+}
+
+template <typename T, typename TB>
+cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
+  const bool bf16 = a.dtype == CCE_BF16;
+  CUtensorMap tmA, tmB;
+  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1};
+  const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
+  DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, a.keep, static_cast<T*>(a.dlogits),
+                        a.grad_bias, a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld,
+                        ceil_div(a.V, kStatTile)};
+  return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
+}
+
+}  // namespace
+
+cudaError_t tc_forward(const FwdArgs& a, cudaStream_t s) {
+  if (a.N == 0 || a.V == 0) return cudaSuccess;
+  switch (a.bias == nullptr ? -1 : a.bias_dtype) {
+    case -1: return fwd_launch<void>(a, s);
+    case CCE_F32: return fwd_launch<float>(a, s);
+    case CCE_F16: return fwd_launch<__half>(a, s);
+    case CCE_BF16: return fwd_launch<__nv_bfloat16>(a, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
+  if (a.N == 0 || a.vc_len == 0) return cudaSuccess;
+  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
+  switch (a.bias == nullptr ? -1 : a.bias_dtype) {
+    case -1: return dl_launch<__nv_bfloat16, void>(a, s);
+    case CCE_F32: return dl_launch<__nv_bfloat16, float>(a, s);
+    case CCE_F16: return dl_launch<__nv_bfloat16, __half>(a, s);
+    case CCE_BF16: return dl_launch<__nv_bfloat16, __nv_bfloat16>(a, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
+                      bool write_out, cudaStream_t s) {
+  if (a.N == 0 || a.D == 0) return cudaSuccess;
+  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
+  CUtensorMap tmA, tmB;
+  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  if (!make_tmap(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tmB, cchunk, true, a.D, a.vc_len, a.D, 64, BK)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1};
+  GradEEpi<__nv_bfloat16> epi{grad_e_acc, static_cast<__nv_bfloat16*>(grad_e_out), a.N, a.D,
+                              accumulate ? 1 : 0, write_out ? 1 : 0};
+  return launch_gemm<false, true>(tmA, tmB, sc, epi, true, s);
+}
+
+cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
+  if (a.vc_len == 0 || a.D == 0) return cudaSuccess;
+  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
+  CUtensorMap tmA, tmB;
+  if (!make_tmap(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, 64, BK)) return cudaErrorInvalidValue;
+  if (!make_tmap(&tmB, a.e, true, a.D, a.N, a.D, 64, BK)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0};
+  GradCEpi<__nv_bfloat16> epi{static_cast<__nv_bfloat16*>(grad_c) + a.vc0 * a.D, a.vc_len, a.D};
+  return launch_gemm<true, true>(tmA, tmB, sc, epi, true, s);
+}
+
+int tc_read_status(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v != 0) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_status, &z, sizeof(int));
+  }
+  return v;
+}
+
 }  // namespace cce

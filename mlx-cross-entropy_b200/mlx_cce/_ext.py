@@ -45,7 +45,7 @@ CCE_NO_FILTER = 16
 FILTER_LOG_EPS = math.log(2.0 ** -12)
 
 EXPORTED_SYMBOLS = (
-    "cce_version", "cce_last_error", "cce_launch_count", "cce_num_stat_tiles",
+    "cce_version", "cce_last_error", "cce_launch_count", "cce_device_status", "cce_num_stat_tiles",
     "cce_forward_workspace_bytes", "cce_forward", "cce_lse_combine",
     "cce_backward_workspace_bytes", "cce_backward",
 )
@@ -67,6 +67,8 @@ def _load():
     lib.cce_last_error.argtypes = []
     lib.cce_launch_count.restype = ctypes.c_uint64
     lib.cce_launch_count.argtypes = []
+    lib.cce_device_status.restype = c_int
+    lib.cce_device_status.argtypes = [c_int]
     lib.cce_num_stat_tiles.restype = c_i64
     lib.cce_num_stat_tiles.argtypes = [c_i64]
     lib.cce_forward_workspace_bytes.restype = c_sz
@@ -90,6 +92,11 @@ lib = _load()
 
 def version() -> int:
     return lib.cce_version()
+
+
+def device_status(reset: bool = False):
+    """Raise RuntimeError if a kernel abandoned a pipeline wait (synchronous)."""
+    _check(lib.cce_device_status(1 if reset else 0), "cce_device_status")
 
 
 def launch_count() -> int:

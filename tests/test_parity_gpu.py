@@ -150,9 +150,10 @@ def test_batched_sequence():
     e = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
     c = (torch.randn(V, D, generator=g) * 0.05).to(torch.bfloat16)
     t = torch.randint(0, V, (B, T), generator=g)
-    got = run(e, c, t, reduction="none")
+    go = torch.randn(B, T, generator=g)
+    got = run(e, c, t, reduction="none", grad_out=go)
     assert got["loss"].shape == (B, T)
-    ref = oracle(e, c, t, reduction="none")
+    ref = oracle(e, c, t, reduction="none", grad_out=go)
     check(got, ref, torch.bfloat16)
 
 
@@ -303,3 +304,9 @@ def test_workload3_golden_and_no_nv_allocation():
     peak = torch.cuda.max_memory_allocated() - base
     io = 2 * (w.N * w.D + w.V * w.D) * 2
     assert peak - io < w.N * w.V * 2 * 0.5, (peak, io)
+
+
+def test_zz_device_status_clean():
+    """No tensor-core kernel abandoned a pipeline wait during this session."""
+    torch.cuda.synchronize()
+    _ext.device_status()
