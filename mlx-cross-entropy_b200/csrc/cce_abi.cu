@@ -223,7 +223,8 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
     return fail(CCE_ERR_ARG, "cce_backward: unknown flag bits 0x%x", flags);
   const bool need_de = flags & CCE_NEED_DE, need_dc = flags & CCE_NEED_DC,
              need_db = flags & CCE_NEED_DBIAS;
-  if ((need_de && !grad_e) || (need_dc && !grad_c) || (need_db && !grad_bias))
+  // A zero-size output may come with a NULL pointer (torch gives empty tensors none).
+  if ((need_de && N > 0 && !grad_e) || (need_dc && V > 0 && !grad_c) || (need_db && V > 0 && !grad_bias))
     return fail(CCE_ERR_ARG, "cce_backward: a requested gradient has a NULL output pointer");
   if (need_db && !bias) return fail(CCE_ERR_ARG, "cce_backward: CCE_NEED_DBIAS without bias");
   if (!need_de && !need_dc && !need_db) return CCE_OK;

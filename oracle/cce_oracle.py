@@ -152,38 +152,49 @@ def backward_full(e, c, lse, targets, d_nll, bias=None):
     return dE, dC, dB
 
 
-def block_keep_mask(z, lse, targets, block_rows, block_cols, log_eps=FILTER_LOG_EPS):
+def block_keep_mask(z, lse, targets, block_rows, block_cols, log_eps=FILTER_LOG_EPS,
+                    row_active=None):
     """Block-skip rule of csrc/cce/cce.metal:190-204 at a given block size.
 
     A (block_rows x block_cols) block is kept when some row in it has its
     target inside the block's columns, or when the block's maximum logit minus
-    that row's LSE is >= ``log_eps``.  Returns keep[n_row_blocks, n_col_blocks].
+    that row's LSE is >= ``log_eps``.  ``row_active`` (optional bool [N])
+    restricts the decision to rows that carry gradient (rows with a zero
+    cotangent contribute nothing either way).  Returns keep[n_row_blocks,
+    n_col_blocks].
     """
     n, V = z.shape
     nb = -(-n // block_rows)
     vb = -(-V // block_cols)
     keep = np.zeros((nb, vb), dtype=bool)
     t = np.asarray(targets).astype(np.int64)
+    act = np.ones(n, dtype=bool) if row_active is None else np.asarray(row_active, dtype=bool)
     for i in range(nb):
         r0, r1 = i * block_rows, min((i + 1) * block_rows, n)
-        zz = z[r0:r1] - _f(lse, np.float64)[r0:r1, None]
+        rows = np.arange(r0, r1)[act[r0:r1]]
+        if rows.size == 0:
+            continue
+        zz = z[rows] - _f(lse, np.float64)[rows, None]
         for j in range(vb):
             c0, c1 = j * block_cols, min((j + 1) * block_cols, V)
-            hit = np.any((t[r0:r1] >= c0) & (t[r0:r1] < c1))
+            hit = np.any((t[rows] >= c0) & (t[rows] < c1))
             big = np.any(zz[:, c0:c1].max(axis=1) >= log_eps)
             keep[i, j] = hit or big
     return keep
 
 
 def backward_filtered(e, c, lse, targets, d_nll, bias=None, block_rows=32, block_cols=32,
-                      log_eps=FILTER_LOG_EPS):
+                      log_eps=FILTER_LOG_EPS, skip_zero_rows=False):
     """Gradients with skipped blocks dropped (cce.metal:190-204 + :276-304).
 
+    ``skip_zero_rows`` leaves rows with d_nll == 0 out of the keep decision
+    (the B200 kernels do; the reference's Metal kernel does not).
     Returns (dE, dC, dBias, skipped_fraction).
     """
     t = np.asarray(targets).astype(np.int64)
     z = logits_f64(e, c, bias)
-    keep = block_keep_mask(z, lse, t, block_rows, block_cols, log_eps)
+    act = (np.asarray(d_nll) != 0) if skip_zero_rows else None
+    keep = block_keep_mask(z, lse, t, block_rows, block_cols, log_eps, row_active=act)
     p = np.exp(z - _f(lse, np.float64)[:, None])
     p[np.arange(z.shape[0]), t] -= 1.0
     mask = np.repeat(np.repeat(keep, block_rows, axis=0), block_cols, axis=1)[: z.shape[0], : z.shape[1]]
