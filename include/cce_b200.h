@@ -119,6 +119,31 @@ CCE_API int cce_forward(const void* e, const void* c, const void* bias, int bias
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * cce_forward_noalloc -- cce_forward for callers that cannot allocate device
+ * memory.  No counterpart in the reference (whose MLX runtime allocates every
+ * buffer itself).
+ *
+ * Same arguments and results as cce_forward minus the workspace: the sum-exp
+ * partials live in a static 16 MiB device array inside this library (held on
+ * every GPU that loads the library, until the process exits).  For callers
+ * that can pass inputs and outputs but own no allocator: a plugin or FFI slot
+ * with a fixed memory contract, or a host that forbids allocation while it
+ * runs.  It calls no cudaMalloc / cudaFree.
+ *   - limit: ceil(V / 128) * N <= 4194304 (e.g. V = 128256, N <= 4185);
+ *     larger calls return CCE_ERR_WORKSPACE and do nothing.
+ *   - the first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - all calls on a device share the array: calls that overlap on the GPU
+ *     (different streams, or different host threads without ordering) race.
+ *     Each call writes every partial it reads, so nothing carries over.
+ */
+CCE_API int cce_forward_noalloc(const void* e, const void* c, const void* bias, int bias_dtype,
+                                const int32_t* targets, int64_t N, int64_t D, int64_t V,
+                                int64_t v_offset, int dtype, float* tile_max, float* lse,
+                                float* tgt, void* stream);
+
+/*
  * cce_lse_combine -- merge P partial (lse, target-logit) rows into one.
  *
  *   part_lse, part_tgt: P rows of N fp32 values, row p starting at

@@ -128,6 +128,13 @@ int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
 
 }  // namespace
 
+namespace cce {
+
+// Records `msg` as this thread's cce_last_error() and returns `code`.
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+}  // namespace cce
+
 extern "C" {
 
 int cce_version(void) { return 100; }

@@ -10,6 +10,9 @@ namespace cce {
 // Counts one kernel launch (cce_launch_count) and returns cudaGetLastError().
 cudaError_t launched();
 
+// Records `msg` as this thread's cce_last_error() and returns `code`.
+int report_error(int code, const char* msg);
+
 struct FwdArgs {
   const void* e;
   const void* c;

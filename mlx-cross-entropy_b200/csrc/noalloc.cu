@@ -1,0 +1,80 @@
+// cce_forward_noalloc: the forward pass for callers that cannot allocate
+// device memory.
+//
+// cce_forward needs a workspace (the per-(vocabulary tile, row) sum-exp
+// partials that the LSE fold reads) which the caller allocates.  Some callers
+// have no way to do that: a host that hands the loss only its input and output
+// buffers (a plugin or FFI slot with a fixed memory contract, a framework
+// hook that forbids allocation while it executes), or code that must not
+// allocate at all.  For them the partials live in a fixed device array owned
+// by this library.
+//
+// The array is a file-scope __device__ symbol of kMaxScratchFloats floats
+// (16 MiB): every GPU that loads the library holds it until the process
+// exits, whether or not this entry point is used.  Host code cannot use the
+// symbol's name as a device address, so the address is looked up once per
+// device with cudaGetSymbolAddress (the set-up below) and passed to the
+// kernels as their workspace pointer.
+#include <atomic>
+#include <cstdio>
+
+#include "kernels.cuh"
+
+namespace {
+
+// Capacity in floats: ceil(V / 128) * N must not exceed it (e.g. V = 128256
+// with N up to 4185, or V = 256000 with N up to 2097).
+constexpr int64_t kMaxScratchFloats = 4ll << 20;
+
+static __device__ __align__(256) float g_fwd_scratch[kMaxScratchFloats];
+
+std::atomic<float*> g_scratch_addr[64];
+
+// Device address of g_fwd_scratch on the current device (looked up on the
+// first call per device, then cached).
+int scratch_address(float** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess)
+    return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: cudaGetDevice failed");
+  if (dev < 0 || dev >= 64)
+    return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: device ordinal out of range");
+  float* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    err = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_fwd_scratch);
+    if (err != cudaSuccess || p == nullptr)
+      return cce::report_error(CCE_ERR_CUDA,
+                               "cce_forward_noalloc: cudaGetSymbolAddress of the static scratch failed");
+    g_scratch_addr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return CCE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cce_forward_noalloc(const void* e, const void* c, const void* bias, int bias_dtype,
+                        const int32_t* targets, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                        int dtype, float* tile_max, float* lse, float* tgt, void* stream) {
+  if (N < 0 || V < 0) return cce::report_error(CCE_ERR_SHAPE, "cce_forward_noalloc: negative size");
+  const int64_t need = cce_num_stat_tiles(V) * N;
+  if (need > kMaxScratchFloats) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "cce_forward_noalloc: ceil(V/128) * N = %lld partials exceed the static scratch of "
+             "%lld floats (16 MiB); use cce_forward with a caller-allocated workspace",
+             (long long)need, (long long)kMaxScratchFloats);
+    return cce::report_error(CCE_ERR_WORKSPACE, msg);
+  }
+  float* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != CCE_OK) return rc;
+  // Every partial the LSE fold reads is written by the forward kernel of the
+  // same call first, so the array needs no clearing between calls.
+  return cce_forward(e, c, bias, bias_dtype, targets, N, D, V, v_offset, dtype, tile_max, lse, tgt,
+                     scratch, (size_t)kMaxScratchFloats * sizeof(float), stream);
+}
+
+}  // extern "C"

@@ -46,7 +46,7 @@ FILTER_LOG_EPS = math.log(2.0 ** -12)
 
 EXPORTED_SYMBOLS = (
     "cce_version", "cce_last_error", "cce_launch_count", "cce_device_status", "cce_num_stat_tiles",
-    "cce_forward_workspace_bytes", "cce_forward", "cce_lse_combine",
+    "cce_forward_workspace_bytes", "cce_forward", "cce_forward_noalloc", "cce_lse_combine",
     "cce_backward_workspace_bytes", "cce_backward",
 )
 
@@ -76,6 +76,9 @@ def _load():
     lib.cce_forward.restype = c_int
     lib.cce_forward.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_int,
                                 c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]
+    lib.cce_forward_noalloc.restype = c_int
+    lib.cce_forward_noalloc.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                        c_int, c_vp, c_vp, c_vp, c_vp]
     lib.cce_lse_combine.restype = c_int
     lib.cce_lse_combine.argtypes = [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp]
     lib.cce_backward_workspace_bytes.restype = c_sz
