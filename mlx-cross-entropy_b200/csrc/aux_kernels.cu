@@ -15,30 +15,50 @@ namespace cce {
 namespace {
 
 constexpr int kCombRows = 32;    // rows per block (threadIdx.x)
-constexpr int kCombSlices = 8;   // partial slices per row (threadIdx.y)
+constexpr int kCombSlices = 32;  // partial slices per row (threadIdx.y)
+
+// Fold (mp, sp) into the running (m, s): s * 2^(m - M) + sp * 2^(mp - M), M = max.
+__device__ __forceinline__ void fold(float& m, float& s, float mp, float sp) {
+  const float M = fmaxf(m, mp);
+  if (M == -INFINITY) return;
+  s = s * exp2f((m - M) * kLog2e) + sp * exp2f((mp - M) * kLog2e);
+  m = M;
+}
 
 __global__ void __launch_bounds__(kCombRows * kCombSlices)
 lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__ part_sum,
                    const float* __restrict__ part_tgt, int64_t P, int64_t N, int64_t ld,
                    float* __restrict__ lse, float* __restrict__ tgt, float* __restrict__ nll) {
-  __shared__ float sm[kCombSlices][kCombRows];
-  __shared__ float ss[kCombSlices][kCombRows];
-  __shared__ float st[kCombSlices][kCombRows];
+  __shared__ float sm[kCombSlices][kCombRows + 1];
+  __shared__ float ss[kCombSlices][kCombRows + 1];
+  __shared__ float st[kCombSlices][kCombRows + 1];
   const int64_t row = (int64_t)blockIdx.x * kCombRows + threadIdx.x;
   float m = -INFINITY, s = 0.f, t = 0.f;
   if (row < N) {
-    for (int64_t p = threadIdx.y; p < P; p += kCombSlices) {
-      const float mp = part_max[p * ld + row];
-      const float sp = part_sum ? part_sum[p * ld + row] : 1.0f;
-      if (part_tgt) t += part_tgt[p * ld + row];
-      if (sp > 0.f) {
-        if (mp > m) {
-          s = s * exp2f((m - mp) * kLog2e) + sp;
-          m = mp;
-        } else {
-          s += sp * exp2f((mp - m) * kLog2e);
-        }
+    int64_t p = threadIdx.y;
+    // four independent partials per step so their loads overlap
+    for (; p + 3 * kCombSlices < P; p += 4 * kCombSlices) {
+      float mp[4], sp[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t q = (p + u * kCombSlices) * ld + row;
+        mp[u] = part_max[q];
+        sp[u] = part_sum ? part_sum[q] : 1.0f;
+        if (part_tgt) t += part_tgt[q];
       }
+      const float M = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), m);
+      if (M != -INFINITY) {
+        float acc = s * exp2f((m - M) * kLog2e);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc += sp[u] * exp2f((mp[u] - M) * kLog2e);
+        s = acc;
+        m = M;
+      }
+    }
+    for (; p < P; p += kCombSlices) {
+      const int64_t q = p * ld + row;
+      fold(m, s, part_max[q], part_sum ? part_sum[q] : 1.0f);
+      if (part_tgt) t += part_tgt[q];
     }
   }
   sm[threadIdx.y][threadIdx.x] = m;
@@ -46,12 +66,9 @@ lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__
   st[threadIdx.y][threadIdx.x] = t;
   __syncthreads();
   if (threadIdx.y == 0 && row < N) {
-    float M = -INFINITY;
-    for (int i = 0; i < kCombSlices; ++i) M = fmaxf(M, sm[i][threadIdx.x]);
-    float S = 0.f, T = 0.f;
+    float M = -INFINITY, S = 0.f, T = 0.f;
     for (int i = 0; i < kCombSlices; ++i) {
-      const float si = ss[i][threadIdx.x];
-      if (si > 0.f) S += si * exp2f((sm[i][threadIdx.x] - M) * kLog2e);
+      fold(M, S, sm[i][threadIdx.x], ss[i][threadIdx.x]);
       T += st[i][threadIdx.x];
     }
     const float L = M + logf(S);

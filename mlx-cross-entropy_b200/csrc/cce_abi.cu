@@ -82,7 +82,7 @@ int check_arch() {
 struct BwdPlan {
   bool tc;
   int64_t vc;        // chunk rows (also the dlogits row stride)
-  size_t keep_bytes, dl_bytes, acc_bytes;
+  size_t keep_bytes, dl_bytes, acc_bytes, counter_bytes;
 };
 
 bool tc_candidate(int dtype, int64_t D) { return dtype == CCE_BF16 && D % 8 == 0; }
@@ -101,10 +101,12 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   p.keep_bytes = align_up((size_t)cce::ceil_div(N, cce::kRowBlock) * (size_t)cce::ceil_div(V, cce::kStatTile));
   p.dl_bytes = align_up((size_t)N * (size_t)vc * (size_t)elt);
   p.acc_bytes = ((flags & CCE_NEED_DE) && !(flags & CCE_DE_F32)) ? align_up((size_t)N * (size_t)D * 4) : 0;
+  // three tile counters per vocabulary chunk for the dynamically scheduled kernels
+  p.counter_bytes = align_up((size_t)cce::ceil_div(V > 0 ? V : 1, vc) * 3 * sizeof(int));
   return p;
 }
 
-size_t plan_bytes(const BwdPlan& p) { return p.keep_bytes + p.dl_bytes + p.acc_bytes; }
+size_t plan_bytes(const BwdPlan& p) { return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -123,6 +125,41 @@ int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
   if (N > (1ll << 31) || V > (1ll << 31) || D > (1ll << 20))
     return fail(CCE_ERR_SHAPE, "sizes out of supported range N=%lld D=%lld V=%lld", (long long)N, (long long)D, (long long)V);
   if (!dtype_ok(dtype)) return fail(CCE_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  return CCE_OK;
+}
+
+// Side streams of the tensor-core backward: grad_e and grad_c of one chunk run
+// concurrently (grad_e on the higher-priority stream, launched first), so
+// grad_c's CTAs take the SMs that grad_e's last partial wave leaves idle.
+// One set per (host thread, device); created on first use, never destroyed.
+struct SideStreams {
+  cudaStream_t se = nullptr, sc = nullptr;
+  cudaEvent_t start = nullptr, ev_l = nullptr, ev_e = nullptr, ev_c = nullptr;
+};
+
+thread_local SideStreams g_side[64];
+
+int side_streams(SideStreams** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(CCE_ERR_CUDA, "device ordinal %d out of range", dev);
+  SideStreams& ss = g_side[dev];
+  if (ss.se == nullptr) {
+    int lo = 0, hi = 0;
+    err = cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetStreamPriorityRange");
+    SideStreams n;
+    if ((err = cudaStreamCreateWithPriority(&n.se, cudaStreamNonBlocking, hi)) != cudaSuccess ||
+        (err = cudaStreamCreateWithPriority(&n.sc, cudaStreamNonBlocking, lo)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.start, cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_l, cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_e, cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_c, cudaEventDisableTiming)) != cudaSuccess)
+      return cuda_fail(err, "creating the backward side streams");
+    ss = n;
+  }
+  *out = &ss;
   return CCE_OK;
 }
 
@@ -259,6 +296,8 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   void* dl = ws + p.keep_bytes;
   float* acc = nullptr;
   if (need_de) acc = (flags & CCE_DE_F32) ? (float*)grad_e : (float*)(ws + p.keep_bytes + p.dl_bytes);
+  int* counters = (int*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes);
+  if (p.tc) CCE_CUDA_CHECK(cudaMemsetAsync(counters, 0, p.counter_bytes, s), "cce_backward memset counters");
 
   CCE_CUDA_CHECK(cce::launch_block_mask(tile_max, lse, targets, d_nll, N, V, v_offset, filter_log_eps,
                                         (flags & CCE_NO_FILTER) != 0, keep, skip_stats, s),
@@ -266,20 +305,44 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
 
   cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, N, D, V, v_offset, dtype,
-                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr};
+                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr};
   const int64_t nchunks = cce::ceil_div(V, p.vc);
+  SideStreams* ss = nullptr;
+  if (p.tc) {
+    rc = side_streams(&ss);
+    if (rc) return rc;
+    // fork: the side streams start after everything enqueued on `s` so far
+    CCE_CUDA_CHECK(cudaEventRecord(ss->start, s), "cce_backward fork");
+    CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->start, 0), "cce_backward fork");
+    CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->start, 0), "cce_backward fork");
+  }
   for (int64_t ch = 0; ch < nchunks; ++ch) {
     a.vc0 = ch * p.vc;
     a.vc_len = (V - a.vc0) < p.vc ? (V - a.vc0) : p.vc;
     const bool last = ch == nchunks - 1;
+    a.counters = counters + 3 * ch;
     if (p.tc) {
+      // dlogits(ch) on `s` overwrites the buffer grad_e / grad_c of chunk ch-1 read
+      if (ch > 0) {
+        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_e, 0), "cce_backward join");
+        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_c, 0), "cce_backward join");
+      }
       CCE_CUDA_CHECK(cce::tc_dlogits(a, s), "cce_backward tc dlogits");
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_l, s), "cce_backward record");
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->ev_l, 0), "cce_backward wait");
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->ev_l, 0), "cce_backward wait");
       if (need_de) {
         const bool write_out = last && !(flags & CCE_DE_F32);
-        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, write_out ? grad_e : nullptr, write_out, s),
+        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, write_out ? grad_e : nullptr, write_out, ss->se),
                        "cce_backward tc grad_e");
       }
-      if (need_dc) CCE_CUDA_CHECK(cce::tc_grad_c(a, grad_c, s), "cce_backward tc grad_c");
+      if (need_dc) CCE_CUDA_CHECK(cce::tc_grad_c(a, grad_c, ss->sc), "cce_backward tc grad_c");
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_e, ss->se), "cce_backward record");
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_c, ss->sc), "cce_backward record");
+      if (last) {
+        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_e, 0), "cce_backward join");
+        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_c, 0), "cce_backward join");
+      }
     } else {
       CCE_CUDA_CHECK(cce::simt_dlogits(a, s), "cce_backward simt dlogits");
       if (need_de) CCE_CUDA_CHECK(cce::simt_grad_e(a, acc, ch > 0, s), "cce_backward simt grad_e");

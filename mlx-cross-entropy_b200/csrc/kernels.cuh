@@ -42,6 +42,7 @@ struct BwdChunkArgs {
   int64_t vc_ld;         // row stride of the dlogits buffer (elements)
   void* dlogits;         // [N][vc_ld], fp32 (SIMT path) or 16-bit (tensor-core path)
   float* grad_bias;      // [V] fp32 or nullptr
+  int* counters;         // 3 zeroed tile counters of this chunk (dlogits, grad_e, grad_c) or nullptr
 };
 
 // ---- auxiliary kernels (aux_kernels.cu) ----

@@ -44,11 +44,15 @@ constexpr uint32_t B_BYTES = BN * BK * 2;   // 32 KB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + 256;
+constexpr int RING = 4;                          // depth of the tile-id ring
+constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-mask slice
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + 256 + SMASK_BYTES;
 
 struct Sched {
   int num_m, num_n, num_kb;
-  int m_fast;  // consecutive tile ids walk M first (1) or N first (0)
+  int m_fast;    // consecutive tile ids walk M first (1) or N first (0)
+  int a3d, b3d;  // MN-major operand loaded as one 3-D box (else one 2-D box per 64 columns)
+  int* counter;  // dynamic scheduling: next tile id (zeroed before the launch); nullptr = static
   __device__ __forceinline__ void coords(int tile, int& mb, int& nb) const {
     if (m_fast) {
       mb = tile % num_m;
@@ -120,7 +124,9 @@ struct FwdEpi {
     float m, s;
   };
 
+  static constexpr bool kMask = false;
   __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
   __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
@@ -198,13 +204,11 @@ struct DlogitsEpi {
     return kr[t0] || (t0 + 1 < nVt && kr[t0 + 1]);
   }
 
-  __device__ __forceinline__ void inactive_tile(int mb, int nb, int r) const {
-    const int64_t row = (int64_t)mb * BM + r;
-    if (row >= N) return;
-    uint4* p = reinterpret_cast<uint4*>(dl + row * ld + (int64_t)nb * BN);
-#pragma unroll 4
-    for (int i = 0; i < BN * 2 / 16; ++i) p[i] = make_uint4(0, 0, 0, 0);
-  }
+  static constexpr bool kMask = false;
+  __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
+
+  // Rejected tiles are not written: the grad GEMMs skip exactly those blocks.
+  __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
   __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
@@ -262,13 +266,23 @@ template <typename T>
 struct GradEEpi {
   float* acc;   // [N, D] fp32 accumulator
   T* out;       // [N, D] final output (write_out)
+  const uint8_t* mask_src;  // keep + vc0 / 128: the chunk's columns of the [nRb][nVt] mask
+  int64_t mask_ld;          // nVt
+  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
   int64_t N, D;
   int accumulate, write_out;
 
   struct State {
     int64_t row, col0;
   };
+  // The mask slice [row block][stat tile of the chunk] is read through `mk`
+  // (shared copy, row stride mld).  K runs over the chunk's vocabulary rows:
+  // K-block kb (64 rows) lies in the chunk's stat tile kb / 2.
+  static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
+    return mk[(int64_t)mb * mld + (kb >> 1)] != 0;
+  }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
@@ -309,12 +323,20 @@ struct GradEEpi {
 template <typename T>
 struct GradCEpi {
   T* out;        // grad_c + vc0 * D
+  const uint8_t* mask_src;  // keep + vc0 / 128
+  int64_t mask_ld;          // nVt
+  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
   int64_t rows, D;
 
   struct State {
     int64_t row, col0;
   };
+  // M tile mb is the chunk's stat tile mb; K-block kb (64 rows) lies in row block kb / 2.
+  static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
+    return mk[(int64_t)(kb >> 1) * mld + mb] != 0;
+  }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
@@ -350,7 +372,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rfull = tempty + 2;      // tile-id ring: published by the producer
+  uint64_t* rempty = rfull + RING;   // released by the MMA thread + 128 epilogue threads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RING);
+  volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* smask = reinterpret_cast<uint8_t*>(full) + 256;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -365,9 +391,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(tfull + a, 1);
       mbar_init(tempty + a, 128);
     }
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(rfull + i, 1);
+      mbar_init(rempty + i, 129);
+    }
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+  }
+  // Filter-mask slice: copied to shared memory when it fits, else read in place.
+  const uint8_t* mk = nullptr;
+  int64_t mld = 0;
+  if constexpr (Epi::kMask) {
+    const int rows = epi.mask_rows, cols = epi.mask_cols;
+    if ((int64_t)rows * cols <= SMASK_BYTES) {
+      for (int rr = warp; rr < rows; rr += kThreads / 32) {
+        const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
+        for (int cc = lane; cc < cols; cc += 32) smask[rr * cols + cc] = __ldg(src + cc);
+      }
+      mk = smask;
+      mld = cols;
+    } else {
+      mk = epi.mask_src;
+      mld = epi.mask_ld;
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -379,31 +426,50 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer + tile scheduler ----------------
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      // the next tile id is fetched one tile ahead so the atomic's latency
+      // overlaps the current tile's loads
+      int next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x;
+      for (int i = 0;; ++i) {
+        const int slot = i & (RING - 1);
+        if (!mbar_wait(rempty + slot, ((i / RING) & 1) ^ 1u, 5)) break;
+        const int tile = next < num_tiles ? next : -1;
+        ring[slot] = tile;
+        mbar_arrive(rfull + slot);
+        if (tile < 0) break;
+        next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (i + 1) * (int)gridDim.x;
         int mb, nb;
         sched.coords(tile, mb, nb);
         if (!epi.tile_active(mb, nb)) continue;
         bool ok = true;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!epi.kb_active(mk, mld, mb, nb, kb)) continue;
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
           const int k0 = kb * BK;
           if (A_MN) {
-            tma_load_2d(a, &tmA, full + stage, mb * BM, k0);
-            tma_load_2d(a + BOX_MN_BYTES, &tmA, full + stage, mb * BM + 64, k0);
+            if (sched.a3d) {
+              tma_load_3d(a, &tmA, full + stage, 0, k0, mb * (BM / 64));
+            } else {
+              tma_load_2d(a, &tmA, full + stage, mb * BM, k0);
+              tma_load_2d(a + BOX_MN_BYTES, &tmA, full + stage, mb * BM + 64, k0);
+            }
           } else {
             tma_load_2d(a, &tmA, full + stage, k0, mb * BM);
           }
           if (B_MN) {
+            if (sched.b3d) {
+              tma_load_3d(b, &tmB, full + stage, 0, k0, nb * (BN / 64));
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
+            }
           } else {
             tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
           }
@@ -422,8 +488,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      // descriptors of stage 0, k-step 0; the start-address field (addr >> 4,
+      // bits 0-13) is advanced by adding byte offsets >> 4
+      const uint64_t adesc0 = A_MN ? smem_desc(smem_u32(sA), BOX_MN_BYTES, 1024)
+                                   : smem_desc(smem_u32(sA), 16, 1024);
+      const uint64_t bdesc0 = B_MN ? smem_desc(smem_u32(sB), BOX_MN_BYTES, 1024)
+                                   : smem_desc(smem_u32(sB), 16, 1024);
+      constexpr uint32_t a_kstep = (A_MN ? 2048u : 32u) >> 4;
+      constexpr uint32_t b_kstep = (B_MN ? 2048u : 32u) >> 4;
+      for (int i = 0;; ++i) {
+        const int slot = i & (RING - 1);
+        if (!mbar_wait(rfull + slot, (i / RING) & 1, 6)) break;
+        const int tile = ring[slot];
+        mbar_arrive(rempty + slot);
+        if (tile < 0) break;
         int mb, nb;
         sched.coords(tile, mb, nb);
         if (!epi.tile_active(mb, nb)) continue;
@@ -431,19 +509,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
+        uint32_t issued = 0;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!epi.kb_active(mk, mld, mb, nb, kb)) continue;
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = a_base + stage * A_BYTES;
-          const uint32_t b_addr = b_base + stage * B_BYTES;
+          const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
+          const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, BOX_MN_BYTES, 1024)
-                                     : smem_desc(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, BOX_MN_BYTES, 1024)
-                                     : smem_desc(b_addr + k * 32, 16, 1024);
-            mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16(d_tmem, ad + k * a_kstep, bd + k * b_kstep, idesc, (issued | (uint32_t)k) != 0 ? 1u : 0u);
+          ++issued;
           mma_commit(empty + stage);
           if (++stage == STAGES) {
             stage = 0;
@@ -463,7 +539,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int r = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int i = 0;; ++i) {
+      const int slot = i & (RING - 1);
+      if (!mbar_wait(rfull + slot, (i / RING) & 1, 7)) break;
+      const int tile = ring[slot];
+      mbar_arrive(rempty + slot);
+      if (tile < 0) break;
       int mb, nb;
       sched.coords(tile, mb, nb);
       if (!epi.tile_active(mb, nb)) {
@@ -472,6 +553,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
       tc_fence_after();
+      bool any_kb = !Epi::kMask;
+      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = epi.kb_active(mk, mld, mb, nb, kb);
       typename Epi::State st;
       epi.begin(st, mb, nb, r);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -479,7 +562,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         __syncwarp();
-        tmem_ld32(tbase + c * 32, v);
+        if (any_kb) {
+          tmem_ld32(tbase + c * 32, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
         epi.chunk(st, c, v);
       }
       epi.end(st);
@@ -550,6 +638,37 @@ bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int6
   return r == CUDA_SUCCESS;
 }
 
+// An MN-major operand [outer][inner] (inner contiguous, a multiple of 64) as a
+// 3-D tensor [inner / 64 groups][outer rows][64]: one box of (64, box_rows,
+// groups) lands in shared memory as `groups` consecutive 64-column slabs of
+// box_rows x 128 bytes -- the same layout as `groups` separate 2-D boxes.
+bool make_tmap_mn3d(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int64_t outer,
+                    int64_t ld, uint32_t box_rows, uint32_t groups) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || inner % 64 != 0) return false;
+  cuuint64_t dims[3] = {64, (cuuint64_t)outer, (cuuint64_t)(inner / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), 128};
+  cuuint32_t box[3] = {64, box_rows, groups};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// MN-major operand map: the 3-D form when the encoder accepts it, else 2-D boxes
+// of 64 columns.  Returns false when neither can be encoded; *is3d tells which.
+bool make_tmap_mn(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int64_t outer,
+                  int64_t ld, uint32_t groups, int* is3d) {
+  if (make_tmap_mn3d(tm, base, bf16, inner, outer, ld, BK, groups)) {
+    *is3d = 1;
+    return true;
+  }
+  *is3d = 0;
+  return make_tmap(tm, base, bf16, inner, outer, ld, 64, BK);
+}
+
 template <bool A_MN, bool B_MN, class Epi>
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sched& s, const Epi& epi,
                         bool bf16, cudaStream_t stream) {
@@ -596,7 +715,7 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   CUtensorMap tmA, tmB;
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1};
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0, nullptr};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
   return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
 }
@@ -608,7 +727,8 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1};
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
+           a.counters ? a.counters + 0 : nullptr};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, a.keep, static_cast<T*>(a.dlogits),
                         a.grad_bias, a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld,
@@ -648,10 +768,14 @@ cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate,
   CUtensorMap tmA, tmB;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
   if (!make_tmap(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, cchunk, true, a.D, a.vc_len, a.D, 64, BK)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1};
-  GradEEpi<__nv_bfloat16> epi{grad_e_acc, static_cast<__nv_bfloat16*>(grad_e_out), a.N, a.D,
-                              accumulate ? 1 : 0, write_out ? 1 : 0};
+  int b3d = 0;
+  if (!make_tmap_mn(&tmB, cchunk, true, a.D, a.vc_len, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
+           a.counters ? a.counters + 1 : nullptr};
+  GradEEpi<__nv_bfloat16> epi{grad_e_acc, static_cast<__nv_bfloat16*>(grad_e_out),
+                              a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
+                              (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                              a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
   return launch_gemm<false, true>(tmA, tmB, sc, epi, true, s);
 }
 
@@ -659,10 +783,15 @@ cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   if (a.vc_len == 0 || a.D == 0) return cudaSuccess;
   if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
   CUtensorMap tmA, tmB;
-  if (!make_tmap(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, 64, BK)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, a.e, true, a.D, a.N, a.D, 64, BK)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0};
-  GradCEpi<__nv_bfloat16> epi{static_cast<__nv_bfloat16*>(grad_c) + a.vc0 * a.D, a.vc_len, a.D};
+  int a3d = 0, b3d = 0;
+  if (!make_tmap_mn(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
+  if (!make_tmap_mn(&tmB, a.e, true, a.D, a.N, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
+           a.counters ? a.counters + 2 : nullptr};
+  GradCEpi<__nv_bfloat16> epi{static_cast<__nv_bfloat16*>(grad_c) + a.vc0 * a.D,
+                              a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
+                              (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                              a.vc_len, a.D};
   return launch_gemm<true, true>(tmA, tmB, sc, epi, true, s);
 }
 

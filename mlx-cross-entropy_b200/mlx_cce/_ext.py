@@ -17,11 +17,13 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from pathlib import Path
 
 import torch
 
-_LIB_PATH = Path(__file__).resolve().parent / "libcce_b200.so"
+# CCE_LIB_PATH may point at another build of the same library (A/B timing).
+_LIB_PATH = Path(os.environ.get("CCE_LIB_PATH") or Path(__file__).resolve().parent / "libcce_b200.so")
 
 CCE_OK = 0
 CCE_ERR_SHAPE = -1
