@@ -320,8 +320,9 @@ def run_ours(args, rank, world, local_rank):
                        "reduction": w.reduction,
                        "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (c is %.2f GB), no flush" % (V * D * 2 / 1e9)},
-            "tflops": tflops, "pct_bf16_peak": tflops / peak_burst,
-            "pct_bf16_peak_sustained": tflops / peak_sus,
+            # whole-job TFLOP/s against the peak of all N GPUs together
+            "tflops": tflops, "pct_bf16_peak": tflops / (peak_burst * world),
+            "pct_bf16_peak_sustained": tflops / (peak_sus * world),
             "flops_per_step": flops,
             "skipped_blocks_frac": (skipped / total) if total else None,
             "fwd_ms": fwd_avg, "bwd_ms": bwd_avg,
