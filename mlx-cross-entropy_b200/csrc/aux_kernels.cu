@@ -123,6 +123,34 @@ __global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n) {
     dst[i] = v;
 }
 
+// One block: s = smallest power of two >= max |x| (exact scaling for fp16
+// dlogits, which then lie in [-1, 1]); s = 1 when every x is zero.
+__global__ void __launch_bounds__(1024) pow2_absmax_kernel(const float* __restrict__ x, int64_t n,
+                                                           float* __restrict__ out) {
+  __shared__ float red[32];
+  float m = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) {
+      float s = 1.f;
+      if (m > 0.f && isfinite(m)) {
+        int ex;
+        const float f = frexpf(m, &ex);  // m = f * 2^ex, f in [0.5, 1)
+        s = ldexpf(1.f, f == 0.5f ? ex - 1 : ex);
+      }
+      out[0] = s;
+      out[1] = 1.f / s;
+    }
+  }
+}
+
 int grid_for(int64_t n, int threads) {
   int64_t b = ceil_div(n, threads);
   if (b > 148 * 16) b = 148 * 16;
@@ -170,6 +198,11 @@ cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, c
     default:
       return cudaErrorInvalidValue;
   }
+  return launched();
+}
+
+cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream) {
+  pow2_absmax_kernel<<<1, 1024, 0, stream>>>(x, n, out);
   return launched();
 }
 

@@ -82,10 +82,10 @@ int check_arch() {
 struct BwdPlan {
   bool tc;
   int64_t vc;        // chunk rows (also the dlogits row stride)
-  size_t keep_bytes, dl_bytes, acc_bytes, counter_bytes;
+  size_t keep_bytes, dl_bytes, acc_bytes, counter_bytes, scale_bytes;
 };
 
-bool tc_candidate(int dtype, int64_t D) { return dtype == CCE_BF16 && D % 8 == 0; }
+bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
 
 BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {
   BwdPlan p{};
@@ -103,10 +103,13 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   p.acc_bytes = ((flags & CCE_NEED_DE) && !(flags & CCE_DE_F32)) ? align_up((size_t)N * (size_t)D * 4) : 0;
   // three tile counters per vocabulary chunk for the dynamically scheduled kernels
   p.counter_bytes = align_up((size_t)cce::ceil_div(V > 0 ? V : 1, vc) * 3 * sizeof(int));
+  p.scale_bytes = (tc && dtype == CCE_F16) ? kAlign : 0;  // {s, 1/s} for fp16 dlogits
   return p;
 }
 
-size_t plan_bytes(const BwdPlan& p) { return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes; }
+size_t plan_bytes(const BwdPlan& p) {
+  return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes;
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -297,7 +300,10 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   float* acc = nullptr;
   if (need_de) acc = (flags & CCE_DE_F32) ? (float*)grad_e : (float*)(ws + p.keep_bytes + p.dl_bytes);
   int* counters = (int*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes);
+  float* scale = p.scale_bytes ? (float*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes)
+                               : nullptr;
   if (p.tc) CCE_CUDA_CHECK(cudaMemsetAsync(counters, 0, p.counter_bytes, s), "cce_backward memset counters");
+  if (scale) CCE_CUDA_CHECK(cce::launch_pow2_absmax(d_nll, N, scale, s), "cce_backward scale");
 
   CCE_CUDA_CHECK(cce::launch_block_mask(tile_max, lse, targets, d_nll, N, V, v_offset, filter_log_eps,
                                         (flags & CCE_NO_FILTER) != 0, keep, skip_stats, s),
@@ -305,7 +311,7 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
 
   cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, N, D, V, v_offset, dtype,
-                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr};
+                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr, scale};
   const int64_t nchunks = cce::ceil_div(V, p.vc);
   SideStreams* ss = nullptr;
   if (p.tc) {

@@ -43,6 +43,7 @@ struct BwdChunkArgs {
   void* dlogits;         // [N][vc_ld], fp32 (SIMT path) or 16-bit (tensor-core path)
   float* grad_bias;      // [V] fp32 or nullptr
   int* counters;         // 3 zeroed tile counters of this chunk (dlogits, grad_e, grad_c) or nullptr
+  const float* scale;    // fp16 tensor-core path: {s, 1/s} with s = 2^ceil(log2 max|d_nll|); else nullptr
 };
 
 // ---- auxiliary kernels (aux_kernels.cu) ----
@@ -56,6 +57,8 @@ cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int
                               float log_eps, bool no_filter, uint8_t* keep, int64_t* skip_stats,
                               cudaStream_t stream);
 cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, cudaStream_t stream);
+// out[0] = s = the power of two >= max |x| (1 if all zero), out[1] = 1 / s
+cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t stream);
 
 // ---- SIMT kernels (simt_kernels.cu): any dtype, any shape ----

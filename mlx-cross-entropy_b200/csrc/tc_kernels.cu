@@ -125,11 +125,11 @@ struct FwdEpi {
   };
 
   static constexpr bool kMask = false;
-  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
   __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
-  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.tl = st.row < N ? (int64_t)targets[st.row] - v_offset : -1;
     st.col0 = (int64_t)nb * BN;
@@ -187,40 +187,44 @@ struct DlogitsEpi {
   const float* lse;
   const float* d_nll;
   const void* bias;
-  const uint8_t* keep;  // [nRb][nVt]
   T* dl;                // [N][ld], column 0 = local vocab row vc0
   float* grad_bias;     // [V] or nullptr
-  int64_t N, V, v_offset, vc0, vc_end, ld, nVt;
+  const float* scale;   // fp16: {s, 1/s}, dl holds w / s; nullptr = unscaled (bf16)
+  const uint8_t* mask_src;  // keep + vc0 / 128: the chunk's columns of the [nRb][nVt] mask
+  int64_t mask_ld;          // nVt
+  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
+  int64_t N, V, v_offset, vc0, vc_end, ld;
 
   struct State {
     int64_t row, tl, col0;
-    float g, L;
+    float g, L, s;  // g = d_nll / s
     bool k0, k1;
   };
 
-  __device__ __forceinline__ bool tile_active(int mb, int nb) const {
-    const int64_t t0 = (vc0 + (int64_t)nb * BN) >> 7;
-    const uint8_t* kr = keep + (int64_t)mb * nVt;
-    return kr[t0] || (t0 + 1 < nVt && kr[t0 + 1]);
+  // The mask slice is read through `mk` (shared copy, row stride mld); the
+  // tile's two 128-column halves are the chunk's stat tiles 2 nb and 2 nb + 1.
+  static constexpr bool kMask = true;
+  __device__ __forceinline__ bool tile_active(const uint8_t* mk, int64_t mld, int mb, int nb) const {
+    const uint8_t* kr = mk + (int64_t)mb * mld;
+    return kr[2 * nb] || (2 * nb + 1 < mask_cols && kr[2 * nb + 1]);
   }
-
-  static constexpr bool kMask = false;
   __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
 
   // Rejected tiles are not written: the grad GEMMs skip exactly those blocks.
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
-  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const uint8_t* mk, int64_t mld, int mb, int nb,
+                                        int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = vc0 + (int64_t)nb * BN;  // local vocab id of the tile's column 0
     const bool ok = st.row < N;
-    st.g = ok ? d_nll[st.row] : 0.f;
+    st.s = scale ? scale[0] : 1.f;
+    st.g = ok ? d_nll[st.row] * (scale ? scale[1] : 1.f) : 0.f;
     st.L = ok ? lse[st.row] : 0.f;
     st.tl = ok ? (int64_t)targets[st.row] - v_offset : -1;
-    const int64_t t0 = st.col0 >> 7;
-    const uint8_t* kr = keep + (int64_t)mb * nVt;
-    st.k0 = kr[t0] != 0;
-    st.k1 = (t0 + 1 < nVt) && kr[t0 + 1] != 0;
+    const uint8_t* kr = mk + (int64_t)mb * mld;
+    st.k0 = kr[2 * nb] != 0;
+    st.k1 = (2 * nb + 1 < mask_cols) && kr[2 * nb + 1] != 0;
   }
 
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
@@ -251,7 +255,7 @@ struct DlogitsEpi {
     if (grad_bias != nullptr) {
       const int lane = threadIdx.x & 31;
       const float colsum = warp_transpose_sum32(v);
-      if (kept && cb + lane < vc_end && colsum != 0.f) atomicAdd(grad_bias + cb + lane, colsum);
+      if (kept && cb + lane < vc_end && colsum != 0.f) atomicAdd(grad_bias + cb + lane, colsum * st.s);
     }
   }
 
@@ -266,6 +270,7 @@ template <typename T>
 struct GradEEpi {
   float* acc;   // [N, D] fp32 accumulator
   T* out;       // [N, D] final output (write_out)
+  const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const uint8_t* mask_src;  // keep + vc0 / 128: the chunk's columns of the [nRb][nVt] mask
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, stat tiles in the chunk
@@ -274,19 +279,21 @@ struct GradEEpi {
 
   struct State {
     int64_t row, col0;
+    float s;
   };
   // The mask slice [row block][stat tile of the chunk] is read through `mk`
   // (shared copy, row stride mld).  K runs over the chunk's vocabulary rows:
   // K-block kb (64 rows) lies in the chunk's stat tile kb / 2.
   static constexpr bool kMask = true;
-  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
   __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
     return mk[(int64_t)mb * mld + (kb >> 1)] != 0;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
-  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
+    st.s = scale ? scale[0] : 1.f;
   }
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
     if (st.row >= N) return;
@@ -298,7 +305,7 @@ struct GradEEpi {
       float* a = acc + st.row * D + col;
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i];
+      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i] * st.s;
       if (accumulate) {
         const float4 x0 = *reinterpret_cast<const float4*>(a);
         const float4 x1 = *reinterpret_cast<const float4*>(a + 4);
@@ -323,6 +330,7 @@ struct GradEEpi {
 template <typename T>
 struct GradCEpi {
   T* out;        // grad_c + vc0 * D
+  const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const uint8_t* mask_src;  // keep + vc0 / 128
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, stat tiles in the chunk
@@ -330,17 +338,19 @@ struct GradCEpi {
 
   struct State {
     int64_t row, col0;
+    float s;
   };
   // M tile mb is the chunk's stat tile mb; K-block kb (64 rows) lies in row block kb / 2.
   static constexpr bool kMask = true;
-  __device__ __forceinline__ bool tile_active(int, int) const { return true; }
+  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
   __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
     return mk[(int64_t)(kb >> 1) * mld + mb] != 0;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
-  __device__ __forceinline__ void begin(State& st, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
+    st.s = scale ? scale[0] : 1.f;
   }
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
     if (st.row >= rows) return;
@@ -349,7 +359,10 @@ struct GradCEpi {
     for (int g = 0; g < 4; ++g) {
       const int64_t col = cb + g * 8;
       if (col >= D) break;
-      store8<T>(out + st.row * D + col, v + g * 8);
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i] * st.s;
+      store8<T>(out + st.row * D + col, o);
     }
   }
   __device__ __forceinline__ void end(State&) const {}
@@ -443,7 +456,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (i + 1) * (int)gridDim.x;
         int mb, nb;
         sched.coords(tile, mb, nb);
-        if (!epi.tile_active(mb, nb)) continue;
+        if (!epi.tile_active(mk, mld, mb, nb)) continue;
         bool ok = true;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
           if (!epi.kb_active(mk, mld, mb, nb, kb)) continue;
@@ -504,7 +517,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (tile < 0) break;
         int mb, nb;
         sched.coords(tile, mb, nb);
-        if (!epi.tile_active(mb, nb)) continue;
+        if (!epi.tile_active(mk, mld, mb, nb)) continue;
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -547,7 +560,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (tile < 0) break;
       int mb, nb;
       sched.coords(tile, mb, nb);
-      if (!epi.tile_active(mb, nb)) {
+      if (!epi.tile_active(mk, mld, mb, nb)) {
         epi.inactive_tile(mb, nb, r);
         continue;
       }
@@ -556,7 +569,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       bool any_kb = !Epi::kMask;
       for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = epi.kb_active(mk, mld, mb, nb, kb);
       typename Epi::State st;
-      epi.begin(st, mb, nb, r);
+      epi.begin(st, mk, mld, mb, nb, r);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -703,8 +716,7 @@ bool tc_supported(const void* e, const void* c, int64_t D, int dtype) {
 }
 
 bool tc_backward_supported(const void* e, const void* c, int64_t D, int dtype) {
-  // fp16 dlogits would underflow (softmax * d_nll below 2^-24): bf16 only.
-  return dtype == CCE_BF16 && tc_supported(e, c, D, dtype);
+  return tc_supported(e, c, D, dtype);
 }
 
 namespace {
@@ -730,9 +742,10 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            a.counters ? a.counters + 0 : nullptr};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
-  DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, a.keep, static_cast<T*>(a.dlogits),
-                        a.grad_bias, a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld,
-                        ceil_div(a.V, kStatTile)};
+  DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
+                        a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
+                        (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                        a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
   return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
 }
 
@@ -749,50 +762,75 @@ cudaError_t tc_forward(const FwdArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
-  if (a.N == 0 || a.vc_len == 0) return cudaSuccess;
-  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
+template <typename T>
+cudaError_t dl_dispatch(const BwdChunkArgs& a, cudaStream_t s) {
   switch (a.bias == nullptr ? -1 : a.bias_dtype) {
-    case -1: return dl_launch<__nv_bfloat16, void>(a, s);
-    case CCE_F32: return dl_launch<__nv_bfloat16, float>(a, s);
-    case CCE_F16: return dl_launch<__nv_bfloat16, __half>(a, s);
-    case CCE_BF16: return dl_launch<__nv_bfloat16, __nv_bfloat16>(a, s);
+    case -1: return dl_launch<T, void>(a, s);
+    case CCE_F32: return dl_launch<T, float>(a, s);
+    case CCE_F16: return dl_launch<T, __half>(a, s);
+    case CCE_BF16: return dl_launch<T, __nv_bfloat16>(a, s);
   }
   return cudaErrorInvalidValue;
 }
 
+cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
+  if (a.N == 0 || a.vc_len == 0) return cudaSuccess;
+  if (a.dtype == CCE_BF16) return dl_dispatch<__nv_bfloat16>(a, s);
+  if (a.dtype == CCE_F16) return dl_dispatch<__half>(a, s);
+  return cudaErrorNotSupported;
+}
+
+namespace {
+
+template <typename T>
+cudaError_t grad_e_launch(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
+                          bool write_out, cudaStream_t s) {
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap tmA, tmB;
+  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  if (!make_tmap(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
+  int b3d = 0;
+  if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
+           a.counters ? a.counters + 1 : nullptr};
+  GradEEpi<T> epi{grad_e_acc, static_cast<T*>(grad_e_out), a.scale,
+                  a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
+                  (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                  a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
+  return launch_gemm<false, true>(tmA, tmB, sc, epi, bf16, s);
+}
+
+template <typename T>
+cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap tmA, tmB;
+  int a3d = 0, b3d = 0;
+  if (!make_tmap_mn(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
+  if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
+           a.counters ? a.counters + 2 : nullptr};
+  GradCEpi<T> epi{static_cast<T*>(grad_c) + a.vc0 * a.D, a.scale,
+                  a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
+                  (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                  a.vc_len, a.D};
+  return launch_gemm<true, true>(tmA, tmB, sc, epi, bf16, s);
+}
+
+}  // namespace
+
 cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
                       bool write_out, cudaStream_t s) {
   if (a.N == 0 || a.D == 0) return cudaSuccess;
-  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
-  CUtensorMap tmA, tmB;
-  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
-  if (!make_tmap(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
-  int b3d = 0;
-  if (!make_tmap_mn(&tmB, cchunk, true, a.D, a.vc_len, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
-           a.counters ? a.counters + 1 : nullptr};
-  GradEEpi<__nv_bfloat16> epi{grad_e_acc, static_cast<__nv_bfloat16*>(grad_e_out),
-                              a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
-                              (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
-                              a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
-  return launch_gemm<false, true>(tmA, tmB, sc, epi, true, s);
+  if (a.dtype == CCE_BF16) return grad_e_launch<__nv_bfloat16>(a, grad_e_acc, accumulate, grad_e_out, write_out, s);
+  if (a.dtype == CCE_F16) return grad_e_launch<__half>(a, grad_e_acc, accumulate, grad_e_out, write_out, s);
+  return cudaErrorNotSupported;
 }
 
 cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   if (a.vc_len == 0 || a.D == 0) return cudaSuccess;
-  if (a.dtype != CCE_BF16) return cudaErrorNotSupported;
-  CUtensorMap tmA, tmB;
-  int a3d = 0, b3d = 0;
-  if (!make_tmap_mn(&tmA, a.dlogits, true, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
-  if (!make_tmap_mn(&tmB, a.e, true, a.D, a.N, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
-           a.counters ? a.counters + 2 : nullptr};
-  GradCEpi<__nv_bfloat16> epi{static_cast<__nv_bfloat16*>(grad_c) + a.vc0 * a.D,
-                              a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
-                              (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
-                              a.vc_len, a.D};
-  return launch_gemm<true, true>(tmA, tmB, sc, epi, true, s);
+  if (a.dtype == CCE_BF16) return grad_c_launch<__nv_bfloat16>(a, grad_c, s);
+  if (a.dtype == CCE_F16) return grad_c_launch<__half>(a, grad_c, s);
+  return cudaErrorNotSupported;
 }
 
 int tc_read_status(bool reset) {

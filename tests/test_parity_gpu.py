@@ -144,6 +144,19 @@ def test_bias(dtype, bias_dtype):
     check(run(e, c, t, bias=b), oracle(e, c, t, bias=b), dtype)
 
 
+def test_fp16_uniform_softmax_backward():
+    """fp16 dlogits are stored scaled by 1 / 2^ceil(log2 max|d_nll|): with a near-uniform
+    softmax over V=32000 and mean reduction the unscaled values (~1e-7) would sit in
+    fp16's subnormal range; scaled they keep full precision."""
+    g = torch.Generator().manual_seed(21)
+    N, D, V = 256, 512, 32000
+    e = torch.randn(N, D, generator=g).half()
+    c = (torch.randn(V, D, generator=g) * 0.02).half()
+    t = torch.randint(0, V, (N,), generator=g)
+    got = run(e, c, t)
+    check(got, oracle(e, c, t), torch.float16)
+
+
 def test_batched_sequence():
     g = torch.Generator().manual_seed(42)
     B, T, D, V = 4, 128, 256, 4096
