@@ -48,7 +48,11 @@ int cuda_fail(cudaError_t err, const char* where) {
   } while (0)
 
 constexpr size_t kAlign = 256;
-constexpr int64_t kDlBudgetBytes = 128ll << 20;  // dlogits chunk buffer budget
+// dlogits chunk buffer: aim for 16384 vocabulary rows per chunk (few launches,
+// little grad_e accumulator traffic) within 1 GiB, and never below 128 MiB.
+constexpr int64_t kDlTargetRows = 16384;
+constexpr int64_t kDlMaxBytes = 1ll << 30;
+constexpr int64_t kDlMinBytes = 128ll << 20;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -93,7 +97,10 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   const int64_t gran = tc ? 256 : 128;
   const int64_t elt = tc ? 2 : 4;
   const int64_t nrow = N > 0 ? N : 1;
-  int64_t vc = (kDlBudgetBytes / (nrow * elt)) / gran * gran;
+  int64_t budget = nrow * elt * kDlTargetRows;
+  if (budget > kDlMaxBytes) budget = kDlMaxBytes;
+  if (budget < kDlMinBytes) budget = kDlMinBytes;
+  int64_t vc = (budget / (nrow * elt)) / gran * gran;
   if (vc < gran) vc = gran;
   const int64_t vmax = cce::round_up(V > 0 ? V : 1, gran);
   if (vc > vmax) vc = vmax;

@@ -45,7 +45,7 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
-constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-mask slice
+constexpr uint32_t SMASK_BYTES = 32768;   // shared copy of the chunk's filter-mask slice
 constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + 256 + SMASK_BYTES;
 
 struct Sched {
@@ -53,16 +53,36 @@ struct Sched {
   int m_fast;    // consecutive tile ids walk M first (1) or N first (0)
   int a3d, b3d;  // MN-major operand loaded as one 3-D box (else one 2-D box per 64 columns)
   int* counter;  // dynamic scheduling: next tile id (zeroed before the launch); nullptr = static
+  int group;     // grouped raster: blocks of the fast dimension per group (<= 0: all)
+  // Tile id -> (mb, nb).  Ids walk the fast dimension inside groups of `group`
+  // blocks, then the slow dimension, then the next group: the ~148 tiles in
+  // flight cover group x (148 / group) blocks, so both operand panels of the
+  // window stay in L2 even when one operand as a whole does not.
   __device__ __forceinline__ void coords(int tile, int& mb, int& nb) const {
+    const int fast = m_fast ? num_m : num_n;
+    const int slow = m_fast ? num_n : num_m;
+    const int gsz0 = (group > 0 && group < fast) ? group : fast;
+    const int per_group = gsz0 * slow;
+    const int g = tile / per_group;
+    const int r = tile - g * per_group;
+    const int gsz = min(gsz0, fast - g * gsz0);
+    const int f = g * gsz0 + r % gsz;
+    const int sl = r / gsz;
     if (m_fast) {
-      mb = tile % num_m;
-      nb = tile / num_m;
+      mb = f;
+      nb = sl;
     } else {
-      nb = tile % num_n;
-      mb = tile / num_n;
+      nb = f;
+      mb = sl;
     }
   }
 };
+
+// Fast-dimension group size: all blocks when that operand fits comfortably in
+// L2 (it is then read from DRAM once however the tiles are ordered), else 16.
+int raster_group(int64_t fast_operand_bytes) {
+  return fast_operand_bytes <= (40ll << 20) ? 0 : 16;
+}
 
 // ---------------------------------------------------------------------------
 // helpers for the epilogues
@@ -727,7 +747,8 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   CUtensorMap tmA, tmB;
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0, nullptr};
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0, nullptr,
+           raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
   return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
 }
@@ -740,7 +761,7 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
-           a.counters ? a.counters + 0 : nullptr};
+           a.counters ? a.counters + 0 : nullptr, raster_group(a.N * a.D * 2)};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
@@ -792,7 +813,7 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* grad_e_acc, bool accumul
   int b3d = 0;
   if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
-           a.counters ? a.counters + 1 : nullptr};
+           a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2)};
   GradEEpi<T> epi{grad_e_acc, static_cast<T*>(grad_e_out), a.scale,
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
@@ -808,7 +829,7 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   if (!make_tmap_mn(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
   if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
-           a.counters ? a.counters + 2 : nullptr};
+           a.counters ? a.counters + 2 : nullptr, raster_group(a.N * a.D * 2)};
   GradCEpi<T> epi{static_cast<T*>(grad_c) + a.vc0 * a.D, a.scale,
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),

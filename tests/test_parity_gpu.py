@@ -335,3 +335,44 @@ def test_zz_device_status_clean():
     """No tensor-core kernel abandoned a pipeline wait during this session."""
     torch.cuda.synchronize()
     _ext.device_status()
+
+
+def test_workload5_full_size_sampled():
+    """Config 5 (N=32768, D=8192, V=128256, bf16, reduction='sum') on one GPU.
+
+    A dense CPU oracle is out of reach (2.75e14 FLOP), so the float64 oracle is
+    evaluated on sampled rows (LSE, target logit, grad_e) and sampled
+    vocabulary rows (grad_c, given the GPU's per-row LSE once its sampled rows
+    are verified)."""
+    e, c, t, bias, go, w = synthetic.make_inputs(5)
+    dev = _dev()
+    N, D, V = w.N, w.D, w.V
+    e2 = e.reshape(N, D)
+    t2 = t.reshape(N)
+    e_ = e2.to(dev).requires_grad_(True)
+    c_ = c.to(dev).requires_grad_(True)
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    loss, lse = mlx_cce.linear_cross_entropy(e_, c_, t2.to(dev), reduction="sum", return_lse=True,
+                                             skip_stats=stats)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert torch.isfinite(loss).item()
+    _ext.device_status()
+    rng = np.random.default_rng(5)
+    rows = np.sort(rng.choice(N, 8, replace=False))
+    safe, valid = O.sanitize(t2.numpy())
+    en = e2.float().numpy()
+    cn = c.float().numpy()
+    lse_ref, tgt_ref = O.rows_lse_tgt(en, cn, safe, rows)
+    lse_gpu = lse.detach().cpu().double().numpy()
+    np.testing.assert_allclose(lse_gpu[rows], lse_ref, rtol=1e-3)
+    d_nll = valid.astype(np.float64)
+    dE_ref = O.rows_grad_e(en, cn, safe, lse_ref, d_nll[rows], rows)
+    dE_gpu = e_.grad[torch.as_tensor(rows, device=dev)].float().cpu().numpy()
+    assert O.rel_max_abs(dE_gpu, dE_ref) < GRAD_TOL
+    cols = np.unique(np.concatenate([rng.choice(V, 6, replace=False), safe[valid][:2]]))
+    dC_ref, _ = O.cols_grad_c(en, cn, safe, lse_gpu, d_nll, cols)
+    dC_gpu = c_.grad[torch.as_tensor(cols, device=dev)].float().cpu().numpy()
+    assert O.rel_max_abs(dC_gpu, dC_ref) < GRAD_TOL
+    skipped, total = stats.tolist()
+    assert total == (N // 128) * _ext.num_stat_tiles(V)
