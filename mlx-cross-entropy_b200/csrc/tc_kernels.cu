@@ -25,6 +25,7 @@
 #include <cuda.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <type_traits>
 
 #include "kernels.cuh"
@@ -225,6 +226,7 @@ struct DlogitsEpi {
   // tile's two 128-column halves are the chunk's stat tiles 2 nb and 2 nb + 1.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const uint8_t* mk, int64_t mld, int mb, int nb) const {
+    if (mb >= mask_rows) return false;
     const uint8_t* kr = mk + (int64_t)mb * mld;
     return kr[2 * nb] || (2 * nb + 1 < mask_cols && kr[2 * nb + 1]);
   }
@@ -243,8 +245,8 @@ struct DlogitsEpi {
     st.L = ok ? lse[st.row] : 0.f;
     st.tl = ok ? (int64_t)targets[st.row] - v_offset : -1;
     const uint8_t* kr = mk + (int64_t)mb * mld;
-    st.k0 = kr[2 * nb] != 0;
-    st.k1 = (2 * nb + 1 < mask_cols) && kr[2 * nb + 1] != 0;
+    st.k0 = mb < mask_rows && kr[2 * nb] != 0;
+    st.k1 = mb < mask_rows && (2 * nb + 1 < mask_cols) && kr[2 * nb + 1] != 0;
   }
 
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
@@ -307,7 +309,7 @@ struct GradEEpi {
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
   __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
-    return mk[(int64_t)mb * mld + (kb >> 1)] != 0;
+    return mb < mask_rows && mk[(int64_t)mb * mld + (kb >> 1)] != 0;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
@@ -364,7 +366,7 @@ struct GradCEpi {
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
   __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
-    return mk[(int64_t)(kb >> 1) * mld + mb] != 0;
+    return mb < mask_cols && mk[(int64_t)(kb >> 1) * mld + mb] != 0;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
@@ -620,6 +622,303 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// the CTA-pair engine (cta_group::2)
+//
+// Clusters of two CTAs on two SMs compute 256 x 256 tiles: CTA r holds rows
+// [128 r, 128 r + 128) of the A slice and columns [128 r, 128 r + 128) of the
+// B slice (32 KB per stage, 6 stages) and accumulates its 128 rows x 256
+// columns in its own TMEM.  The leader (rank 0) issues every
+// tcgen05.mma.cta_group::2; both CTAs' TMA loads complete on the leader's
+// `full` barrier; the leader's commits arrive on each CTA's own `empty` and
+// `tfull` barriers; both epilogues release the accumulator on the leader's
+// `tempty`.  Tile ids come from the leader's producer, which writes them into
+// both CTAs' rings (distributed shared memory).  Per SM this halves the B
+// traffic of the 1-CTA engine for the same FLOPs.
+// ---------------------------------------------------------------------------
+
+constexpr int STAGES2 = 6;
+constexpr uint32_t A2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 rows of A
+constexpr uint32_t B2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 columns of B
+constexpr uint32_t STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr size_t SMEM2_BYTES = 1024 + STAGES2 * (size_t)STAGE2_BYTES + 256 + SMASK_BYTES;
+
+template <bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const Sched sched, const Epi epi, const uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * A2_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES2 * B2_BYTES);
+  uint64_t* empty = full + STAGES2;
+  uint64_t* tfull = empty + STAGES2;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* rfull = tempty + 2;
+  uint64_t* rempty = rfull + RING;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RING);
+  volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* smask = reinterpret_cast<uint8_t*>(full) + 256;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t peer = rank ^ 1u;
+  const int num_tiles = sched.num_m * sched.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 256);   // both CTAs' epilogue threads
+    }
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(rfull + i, 1);
+      mbar_init(rempty + i, 258);   // leader MMA + 2 x 128 epilogue + peer producer
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  const uint8_t* mk = nullptr;
+  int64_t mld = 0;
+  if constexpr (Epi::kMask) {
+    const int rows = epi.mask_rows, cols = epi.mask_cols;
+    if ((int64_t)rows * cols <= SMASK_BYTES) {
+      for (int rr = warp; rr < rows; rr += kThreads / 32) {
+        const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
+        for (int cc = lane; cc < cols; cc += 32) smask[rr * cols + cc] = __ldg(src + cc);
+      }
+      mk = smask;
+      mld = cols;
+    } else {
+      mk = epi.mask_src;
+      mld = epi.mask_ld;
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // the peer's barriers are initialised before any remote access
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // A pair tile is active / has an active K-block when either CTA's half does.
+  auto tile_on = [&](int mb, int nb) {
+    return epi.tile_active(mk, mld, 2 * mb, nb) || epi.tile_active(mk, mld, 2 * mb + 1, nb);
+  };
+  auto kb_on = [&](int mb, int nb, int kb) {
+    return epi.kb_active(mk, mld, 2 * mb, nb, kb) || epi.kb_active(mk, mld, 2 * mb + 1, nb, kb);
+  };
+  const uint32_t full_leader = mapa_shared(smem_u32(full), 0);   // + 8 * stage
+  const uint32_t rempty_leader = mapa_shared(smem_u32(rempty), 0);
+  const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+
+  if (warp == 0) {
+    // ---------------- TMA producers (both CTAs); tile scheduler (leader) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int next = leader ? (sched.counter ? atomicAdd(sched.counter, 1) : (int)(blockIdx.x >> 1)) : 0;
+      const uint32_t ring_peer = mapa_shared(smem_u32((const void*)ring), peer);
+      const uint32_t rfull_peer = mapa_shared(smem_u32(rfull), peer);
+      for (int i = 0;; ++i) {
+        const int slot = i & (RING - 1);
+        const uint32_t rpar = (i / RING) & 1;
+        int tile;
+        if (leader) {
+          if (!mbar_wait(rempty + slot, rpar ^ 1u, 5)) break;
+          tile = next < num_tiles ? next : -1;
+          ring[slot] = tile;
+          st_cluster_u32(ring_peer + 4 * slot, (uint32_t)tile);
+          mbar_arrive(rfull + slot);
+          mbar_arrive_cluster(rfull_peer + 8 * slot);
+          if (tile >= 0)
+            next = sched.counter ? atomicAdd(sched.counter, 1)
+                                 : (int)(blockIdx.x >> 1) + (i + 1) * (int)(gridDim.x >> 1);
+        } else {
+          if (!mbar_wait_cluster(rfull + slot, rpar, 5)) break;
+          tile = ring[slot];
+          mbar_arrive_cluster(rempty_leader + 8 * slot);
+        }
+        if (tile < 0) break;
+        int mb, nb;
+        sched.coords(tile, mb, nb);
+        if (!tile_on(mb, nb)) continue;
+        bool ok = true;
+        const int arow = mb * 256 + (int)rank * 128;   // this CTA's A rows (or MN columns)
+        const int bcol = nb * 256 + (int)rank * 128;   // this CTA's B columns
+        for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!kb_on(mb, nb, kb)) continue;
+          if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(full + stage, 2 * STAGE2_BYTES);
+          const uint32_t fb = full_leader + 8 * stage;
+          uint8_t* a = sA + stage * A2_BYTES;
+          uint8_t* b = sB + stage * B2_BYTES;
+          const int k0 = kb * BK;
+          if (A_MN) {
+            if (sched.a3d) {
+              tma_load_3d_pair(a, &tmA, fb, 0, k0, arow / 64);
+            } else {
+              tma_load_2d_pair(a, &tmA, fb, arow, k0);
+              tma_load_2d_pair(a + BOX_MN_BYTES, &tmA, fb, arow + 64, k0);
+            }
+          } else {
+            tma_load_2d_pair(a, &tmA, fb, k0, arow);
+          }
+          if (B_MN) {
+            if (sched.b3d) {
+              tma_load_3d_pair(b, &tmB, fb, 0, k0, bcol / 64);
+            } else {
+              tma_load_2d_pair(b, &tmB, fb, bcol, k0);
+              tma_load_2d_pair(b + BOX_MN_BYTES, &tmB, fb, bcol + 64, k0);
+            }
+          } else {
+            tma_load_2d_pair(b, &tmB, fb, k0, bcol);
+          }
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      const uint64_t adesc0 = A_MN ? smem_desc(smem_u32(sA), BOX_MN_BYTES, 1024)
+                                   : smem_desc(smem_u32(sA), 16, 1024);
+      const uint64_t bdesc0 = B_MN ? smem_desc(smem_u32(sB), BOX_MN_BYTES, 1024)
+                                   : smem_desc(smem_u32(sB), 16, 1024);
+      constexpr uint32_t a_kstep = (A_MN ? 2048u : 32u) >> 4;
+      constexpr uint32_t b_kstep = (B_MN ? 2048u : 32u) >> 4;
+      const uint32_t empty_peer = mapa_shared(smem_u32(empty), peer);
+      const uint32_t empty_self = mapa_shared(smem_u32(empty), rank);
+      const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), peer);
+      const uint32_t tfull_self = mapa_shared(smem_u32(tfull), rank);
+      for (int i = 0;; ++i) {
+        const int slot = i & (RING - 1);
+        if (!mbar_wait(rfull + slot, (i / RING) & 1, 6)) break;
+        const int tile = ring[slot];
+        mbar_arrive(rempty + slot);
+        if (tile < 0) break;
+        int mb, nb;
+        sched.coords(tile, mb, nb);
+        if (!tile_on(mb, nb)) continue;
+        if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        uint32_t issued = 0;
+        for (int kb = 0; kb < sched.num_kb; ++kb) {
+          if (!kb_on(mb, nb, kb)) continue;
+          if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = adesc0 + (uint64_t)((stage * A2_BYTES) >> 4);
+          const uint64_t bd = bdesc0 + (uint64_t)((stage * B2_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_f16_pair(d_tmem, ad + k * a_kstep, bd + k * b_kstep, idesc,
+                         (issued | (uint32_t)k) != 0 ? 1u : 0u);
+          ++issued;
+          mma_commit_pair(empty_self + 8 * stage);
+          mma_commit_pair(empty_peer + 8 * stage);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(tfull_self + 8 * acc);
+        mma_commit_pair(tfull_peer + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int i = 0;; ++i) {
+      const int slot = i & (RING - 1);
+      const uint32_t rpar = (i / RING) & 1;
+      int tile;
+      if (leader) {
+        if (!mbar_wait(rfull + slot, rpar, 7)) break;
+        tile = ring[slot];
+        mbar_arrive(rempty + slot);
+      } else {
+        if (!mbar_wait_cluster(rfull + slot, rpar, 7)) break;
+        tile = ring[slot];
+        mbar_arrive_cluster(rempty_leader + 8 * slot);
+      }
+      if (tile < 0) break;
+      int mb, nb;
+      sched.coords(tile, mb, nb);
+      const int vmb = 2 * mb + (int)rank;   // this CTA's 128-row block
+      if (!tile_on(mb, nb)) {
+        epi.inactive_tile(vmb, nb, r);
+        continue;
+      }
+      if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
+      tc_fence_after();
+      bool any_kb = !Epi::kMask;
+      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = kb_on(mb, nb, kb);
+      typename Epi::State st;
+      epi.begin(st, mk, mld, vmb, nb, r);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();
+        if (any_kb) {
+          tmem_ld32(tbase + c * 32, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        epi.chunk(st, c, v);
+      }
+      epi.end(st);
+      __syncwarp();
+      tc_fence_before();
+      if (leader) {
+        mbar_arrive(tempty + acc);
+      } else {
+        mbar_arrive_cluster(tempty_leader + 8 * acc);
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // neither CTA leaves while the other may still touch its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -723,6 +1022,53 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sc
   return launched();
 }
 
+template <bool A_MN, bool B_MN, class Epi>
+cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sched& s, const Epi& epi,
+                         bool bf16, cudaStream_t stream) {
+  auto kern = tc_gemm2_kernel<A_MN, B_MN, Epi>;
+  static std::atomic<int> attr_done[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+    if (err != cudaSuccess) return err;
+    if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
+  }
+  const int tiles = s.num_m * s.num_n;
+  if (tiles == 0) return cudaSuccess;
+  const int pairs = num_sms() / 2;
+  const int grid = 2 * (tiles < pairs ? tiles : pairs);
+  const uint32_t idesc = instr_desc(256, BN, bf16, A_MN, B_MN);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM2_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, s, epi, idesc);
+  if (err != cudaSuccess) return err;
+  return launched();
+}
+
+// CCE_TC_PAIR=1 selects the CTA-pair engine.  It passes the same tests but
+// measured no faster than the single-CTA engine on B200 (both run into the
+// 1 kW power cap, at ~1.5 GHz, with the tensor pipe ~86% busy), so the
+// single-CTA engine is the default.
+bool use_pair() {
+  static const bool v = [] {
+    const char* e = getenv("CCE_TC_PAIR");
+    return e != nullptr && e[0] == '1';
+  }();
+  return v;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -745,11 +1091,13 @@ template <typename TB>
 cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
   CUtensorMap tmA, tmB;
+  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0, nullptr,
-           raster_group(a.N * a.D * 2)};
+  if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, pair ? BN / 2 : BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
+           nullptr, raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
+  if (pair) return launch_gemm2<false, false>(tmA, tmB, sc, epi, bf16, s);
   return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
 }
 
@@ -758,15 +1106,17 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
   CUtensorMap tmA, tmB;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
+  if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, pair ? BN / 2 : BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            a.counters ? a.counters + 0 : nullptr, raster_group(a.N * a.D * 2)};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                         a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
+  if (pair) return launch_gemm2<false, false>(tmA, tmB, sc, epi, bf16, s);
   return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
 }
 
@@ -809,15 +1159,18 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* grad_e_acc, bool accumul
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tmA, tmB;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
   int b3d = 0;
-  if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
+  if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, (pair ? BN / 2 : BN) / 64, &b3d))
+    return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
            a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2)};
   GradEEpi<T> epi{grad_e_acc, static_cast<T*>(grad_e_out), a.scale,
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                   a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
+  if (pair) return launch_gemm2<false, true>(tmA, tmB, sc, epi, bf16, s);
   return launch_gemm<false, true>(tmA, tmB, sc, epi, bf16, s);
 }
 
@@ -826,14 +1179,16 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tmA, tmB;
   int a3d = 0, b3d = 0;
+  const bool pair = use_pair();
   if (!make_tmap_mn(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
-  if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, BN / 64, &b3d)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
+  if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, (pair ? BN / 2 : BN) / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.vc_len, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
            a.counters ? a.counters + 2 : nullptr, raster_group(a.N * a.D * 2)};
   GradCEpi<T> epi{static_cast<T*>(grad_c) + a.vc0 * a.D, a.scale,
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                   a.vc_len, a.D};
+  if (pair) return launch_gemm2<true, true>(tmA, tmB, sc, epi, bf16, s);
   return launch_gemm<true, true>(tmA, tmB, sc, epi, bf16, s);
 }
 
