@@ -231,30 +231,55 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         return float(tt.item())
 
-    for _ in range(args.warmup):
-        step(e, t)
+    # warm-up on a side stream (as CUDA-graph capture wants), then capture one
+    # whole fwd+bwd step; every replay recomputes everything from e, c, targets
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(args.warmup):
+            step(e, t)
+    torch.cuda.current_stream().wait_stream(side)
     barrier()
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(e, t)
+        barrier()
 
-    # ---- device-resident timed region ----
+    # ---- device-resident timed region: graph replays (eager steps with --no-graph) ----
     sampler = ClockSampler()
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
-    skip.zero_()
-    launches0 = _ext.launch_count()
-    _ext.set_timing(True)
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
-        step(e, t)
+        if graph is not None:
+            graph.replay()
+        else:
+            step(e, t)
     ev1.record()
     torch.cuda.synchronize()
     elapsed_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = sampler.stop(set(range(world))) if rank == 0 else None
+
+    # ---- eager timed region: per-call kernel times, launches, skipped blocks ----
+    skip.zero_()
+    launches0 = _ext.launch_count()
+    _ext.set_timing(True)
+    barrier()
+    ev4, ev5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev4.record()
+    for _ in range(args.steps):
+        step(e, t)
+    ev5.record()
+    torch.cuda.synchronize()
+    eager_ms = max_over_ranks(ev4.elapsed_time(ev5))
     launches = _ext.launch_count() - launches0
     recs = _ext.timings()
     _ext.set_timing(False)
-    clocks = sampler.stop(set(range(world))) if rank == 0 else None
     fwd_ms = [a.elapsed_time(b) for name, a, b in recs if name == "forward"]
     bwd_ms = [a.elapsed_time(b) for name, a, b in recs if name == "backward"]
     fwd_avg = max_over_ranks(statistics.mean(fwd_ms)) if fwd_ms else float("nan")
@@ -334,13 +359,22 @@ def run_ours(args, rank, world, local_rank):
                          "algorithmic_bytes": 2.0 * (N * D + vl * D) + 8.0 * N * (-(-vl // 128))},
             "e2e": {"value": N * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            # library kernels per K steps (counted in the eager region; a graph
+            # replay launches the same kernels)
             "gpu_launches": int(launches),
+            "timing": ("CUDA-graph replay of the whole fwd+bwd step" if graph is not None
+                       else "eager steps"),
+            "eager_ms_per_step": eager_ms / args.steps,
             "clocks": clocks,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    # a graph holding NCCL calls must be released before the process group
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
@@ -355,6 +389,7 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=256,
                     help="rows of the workload in one CPU-reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of graph replays")
     ap.add_argument("--N", type=int, default=None, help="scaled-down rows (profiling captures)")
     ap.add_argument("--V", type=int, default=None, help="scaled-down vocabulary (profiling captures)")
     ap.add_argument("--D", type=int, default=None, help="scaled-down hidden size (profiling captures)")

@@ -255,6 +255,45 @@ def test_filter_matches_same_granularity_oracle_and_no_filter_is_exact():
     check(got_exact, ref, torch.bfloat16, grad_tol=1e-2)
 
 
+def test_cuda_graph_capture_matches_eager():
+    """fwd + bwd through the public API captured in a CUDA graph (side-stream
+    fork/join and workspace memsets included) and replayed on new input values
+    equals eager execution on those values."""
+    dev = _dev()
+    e0, c0, t0, b0 = small(384, 128, 3000, torch.bfloat16, seed=31, bias=torch.float32, ignore=0.1)
+    e1, c1, t1, b1 = small(384, 128, 3000, torch.bfloat16, seed=32, bias=torch.float32, ignore=0.1)
+    e = e0.to(dev).requires_grad_(True)
+    c = c0.to(dev).requires_grad_(True)
+    b = b0.to(dev).requires_grad_(True)
+    t = t0.to(dev)
+
+    def step():
+        loss = mlx_cce.linear_cross_entropy(e, c, t, b)
+        loss.backward()
+        return loss
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            e.grad = c.grad = b.grad = None
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    e.grad = c.grad = b.grad = None
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        static_loss = step()
+    with torch.no_grad():
+        e.copy_(e1.to(dev)); c.copy_(c1.to(dev)); b.copy_(b1.to(dev)); t.copy_(t1.to(dev))
+    g.replay()
+    torch.cuda.synchronize()
+    got = dict(loss=static_loss.detach().cpu().double().numpy(),
+               dE=e.grad.cpu().double().numpy(), dC=c.grad.cpu().double().numpy(),
+               dB=b.grad.cpu().double().numpy())
+    check(got, oracle(e1, c1, t1, bias=b1), torch.bfloat16)
+    del g
+
+
 # --- vocabulary sharding, emulated on one GPU ---
 
 @pytest.mark.parametrize("world", [2, 3, 8])
