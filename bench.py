@@ -146,14 +146,20 @@ def cpu_reference_step_fn(cfg, rows):
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    rows = args.ref_rows
-    step, sample, cores, w = cpu_reference_step_fn(args.config, rows)
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
+    # torchrun limits every process to one OpenMP thread; the CPU reference
+    # runs alone on rank 0 and may use every host thread
+    from threadpoolctl import threadpool_limits
+    ncpu = os.cpu_count() or 1
+    torch.set_num_threads(ncpu)
+    with threadpool_limits(limits=ncpu):
+        rows = args.ref_rows
+        step, sample, cores, w = cpu_reference_step_fn(args.config, rows)
+        for _ in range(args.warmup):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        dt = (time.perf_counter() - t0) / args.steps
     value = rows / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
