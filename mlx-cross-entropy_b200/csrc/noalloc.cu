@@ -10,7 +10,7 @@
 // by this library.
 //
 // The array is a file-scope __device__ symbol of kMaxScratchFloats floats
-// (16 MiB): every GPU that loads the library holds it until the process
+// (32 MiB): every GPU that loads the library holds it until the process
 // exits, whether or not this entry point is used.  Host code cannot use the
 // symbol's name as a device address, so the address is looked up once per
 // device with cudaGetSymbolAddress (the set-up below) and passed to the
@@ -22,9 +22,9 @@
 
 namespace {
 
-// Capacity in floats: ceil(V / 128) * N must not exceed it (e.g. V = 128256
+// Capacity in floats: ceil(V / 64) * N must not exceed it (e.g. V = 128256
 // with N up to 4185, or V = 256000 with N up to 2097).
-constexpr int64_t kMaxScratchFloats = 4ll << 20;
+constexpr int64_t kMaxScratchFloats = 8ll << 20;
 
 static __device__ __align__(256) float g_fwd_scratch[kMaxScratchFloats];
 
@@ -63,8 +63,8 @@ int cce_forward_noalloc(const void* e, const void* c, const void* bias, int bias
   if (need > kMaxScratchFloats) {
     char msg[256];
     snprintf(msg, sizeof(msg),
-             "cce_forward_noalloc: ceil(V/128) * N = %lld partials exceed the static scratch of "
-             "%lld floats (16 MiB); use cce_forward with a caller-allocated workspace",
+             "cce_forward_noalloc: ceil(V/64) * N = %lld partials exceed the static scratch of "
+             "%lld floats (32 MiB); use cce_forward with a caller-allocated workspace",
              (long long)need, (long long)kMaxScratchFloats);
     return cce::report_error(CCE_ERR_WORKSPACE, msg);
   }

@@ -94,28 +94,40 @@ simt_fwd_kernel(const T* __restrict__ e, const T* __restrict__ c, const void* __
     const int64_t v = v0 + tx + 16 * j;
     bv[j] = (bias != nullptr && v < V) ? bias_at<TB>(bias, v) : 0.f;
   }
+  // columns tx + 16 j: j < 4 lie in the tile's first 64-column statistics
+  // tile, j >= 4 in the second
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t row = r0 + ty + 16 * i;
     float x[8];
-    float m = -INFINITY;
+    float m[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int64_t v = v0 + tx + 16 * j;
       x[j] = (v < V) ? acc[i][j] + bv[j] : -INFINITY;
-      m = fmaxf(m, x[j]);
+      m[j >> 2] = fmaxf(m[j >> 2], x[j]);
     }
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
+    for (int g = 0; g < 2; ++g)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s += exp2f((x[j] - m) * kLog2e);
+      for (int o = 8; o >= 1; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
+    float s[2] = {0.f, 0.f};
 #pragma unroll
-    for (int o = 8; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    for (int j = 0; j < 8; ++j)
+      if (m[j >> 2] != -INFINITY) s[j >> 2] += exp2f((x[j] - m[j >> 2]) * kLog2e);
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
     if (row < N) {
       if (tx == 0) {
-        tile_max[tile * N + row] = m;
-        tile_sum[tile * N + row] = s;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (v0 + g * kStatTile < V) {
+            tile_max[(2 * tile + g) * N + row] = m[g];
+            tile_sum[(2 * tile + g) * N + row] = s[g];
+          }
+        }
       }
       const int64_t tl = (int64_t)targets[row] - v_offset;
 #pragma unroll
@@ -137,8 +149,11 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
   const int64_t vend = min(vc0 + vc_len, V);
   const int64_t nVt = ceil_div(V, kStatTile);
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const bool kept = keep[(r0 / kRowBlock) * nVt + v0 / kStatTile] != 0;
-  if (!kept) {
+  // the tile's two 64-column statistics tiles
+  const uint8_t* kr = keep + (r0 / kRowBlock) * nVt + v0 / kStatTile;
+  const bool kept0 = kr[0] != 0;
+  const bool kept1 = (v0 / kStatTile + 1 < nVt) && kr[1] != 0;
+  if (!kept0 && !kept1) {
     for (int idx = threadIdx.x; idx < BM * BN; idx += THREADS) {
       const int r = idx / BN, cc = idx % BN;
       const int64_t row = r0 + r, v = v0 + cc;
@@ -173,8 +188,11 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
     for (int j = 0; j < 8; ++j) {
       const int64_t v = v0 + tx + 16 * j;
       if (v < vend) {
-        float w = g * exp2f((acc[i][j] + bv[j] - L) * kLog2e);
-        if (v == tl) w -= g;
+        float w = 0.f;
+        if (j < 4 ? kept0 : kept1) {
+          w = g * exp2f((acc[i][j] + bv[j] - L) * kLog2e);
+          if (v == tl) w -= g;
+        }
         dl[row * ld + (v - vc0)] = w;
         cs[j] += w;
       }

@@ -46,8 +46,9 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
-constexpr uint32_t SMASK_BYTES = 32768;   // shared copy of the chunk's filter-mask slice
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + 256 + SMASK_BYTES;
+constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-mask slice (bits)
+constexpr uint32_t OUT_STAGE_BYTES = 4 * 4096;  // epilogue output staging, 4 KB per epilogue warp
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
 
 struct Sched {
   int num_m, num_n, num_kb;
@@ -85,22 +86,23 @@ int raster_group(int64_t fast_operand_bytes) {
   return fast_operand_bytes <= (40ll << 20) ? 0 : 16;
 }
 
+// Read-only view of a vocabulary chunk's filter-mask slice [row block][stat
+// tile]: bits in shared memory (row-aligned 32-bit words, `wpr` per row) when
+// they fit, else the bytes in global memory (row stride `ld`).
+struct MaskView {
+  const uint32_t* bits;
+  const uint8_t* bytes;
+  int64_t ld;
+  int wpr;
+  __device__ __forceinline__ bool get(int r, int c) const {
+    if (bits) return (bits[r * wpr + (c >> 5)] >> (c & 31)) & 1u;
+    return bytes[(int64_t)r * ld + c] != 0;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // helpers for the epilogues
 // ---------------------------------------------------------------------------
-
-template <typename T>
-__device__ __forceinline__ void store8(T* dst, const float* v) {
-  // 8 16-bit values = one 16-byte store
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    T lo = from_f32<T>(v[2 * i]), hi = from_f32<T>(v[2 * i + 1]);
-    w[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) |
-           ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-  }
-  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-}
 
 // 32 bias values for columns [col0, col0 + 32), zero past `limit`.
 template <typename TB>
@@ -127,6 +129,79 @@ __device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
   return v[0];
 }
 
+// Output staging of one epilogue warp: two 2 KB slots, each 32 rows x 64 bytes
+// in the TMA 64-byte swizzle (16-byte unit u of row r sits at unit
+// u ^ ((r >> 1) & 3), so a warp's 16-byte stores are free of bank conflicts).
+// A filled slot goes to global memory as one TMA box store (or reduce-add)
+// issued by lane 0, which also owns the bulk groups and their waits; the
+// tensor map clips rows and columns past the output's extent.
+struct Stager {
+  const CUtensorMap* tm;
+  uint8_t* buf;  // this warp's 4 KB (1 KB aligned)
+  int slot;      // next slot of a 16-bit store
+
+  __device__ __forceinline__ uint4* unit(int sl, int u) const {
+    const int lane = threadIdx.x & 31;
+    return reinterpret_cast<uint4*>(buf + sl * 2048 + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4));
+  }
+  // All lanes' shared-memory writes become visible to the TMA unit.
+  __device__ __forceinline__ void publish() const {
+    fence_proxy_async();
+    __syncwarp();
+  }
+  // Slot reuse: wait until at most `N` committed groups still read shared memory.
+  template <int N>
+  __device__ __forceinline__ void acquire() const {
+    if ((threadIdx.x & 31) == 0) bulk_wait_read<N>();
+    __syncwarp();
+  }
+  __device__ __forceinline__ void drain() const {
+    if ((threadIdx.x & 31) == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  // 32 values of this lane's row -> one 32 x 32 box of 16-bit T at (x, y).
+  template <typename T>
+  __device__ __forceinline__ void store16(const float (&v)[32], int x, int y) {
+    acquire<1>();  // the slot's previous box (two stores back) has been read
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      T lo = from_f32<T>(v[2 * i]), hi = from_f32<T>(v[2 * i + 1]);
+      w[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) *unit(slot, u) = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+    publish();
+    if ((threadIdx.x & 31) == 0) {
+      tma_store_2d(tm, smem_u32(buf + slot * 2048), x, y);
+      bulk_commit();
+    }
+    slot ^= 1;
+  }
+
+  // 32 fp32 values of this lane's row -> two 16 x 32 boxes at (x, y) and
+  // (x + 16, y), stored or added to global memory.
+  __device__ __forceinline__ void store_f32(const float (&v)[32], int x, int y, bool add) {
+    acquire<0>();
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *unit(h, u) = make_uint4(__float_as_uint(v[16 * h + 4 * u]), __float_as_uint(v[16 * h + 4 * u + 1]),
+                                 __float_as_uint(v[16 * h + 4 * u + 2]), __float_as_uint(v[16 * h + 4 * u + 3]));
+    publish();
+    if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (add) tma_reduce_add_2d(tm, smem_u32(buf + h * 2048), x + 16 * h, y);
+        else tma_store_2d(tm, smem_u32(buf + h * 2048), x + 16 * h, y);
+      }
+      bulk_commit();
+    }
+  }
+};
+
 // ---------------------------------------------------------------------------
 // K1: forward tile statistics
 // ---------------------------------------------------------------------------
@@ -146,11 +221,11 @@ struct FwdEpi {
   };
 
   static constexpr bool kMask = false;
-  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
-  __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
+  __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
-  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.tl = st.row < N ? (int64_t)targets[st.row] - v_offset : -1;
     st.col0 = (int64_t)nb * BN;
@@ -158,7 +233,7 @@ struct FwdEpi {
     st.s = 0.f;
   }
 
-  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
     const int64_t cb = st.col0 + c * 32;
     float b[32];
     if constexpr (!std::is_void<TB>::value) {
@@ -183,10 +258,10 @@ struct FwdEpi {
       st.s = st.s * exp2f(fmaf(st.m, kLog2e, -nml)) + acc;
       st.m = nm;
     }
-    if ((c & 3) == 3) {
-      const int h = c >> 2;
-      if (st.row < N && st.col0 + h * 128 < V) {
-        const int64_t idx = ((st.col0 >> 7) + h) * N + st.row;
+    if ((c & 1) == 1) {  // end of a 64-column statistics tile
+      const int h = c >> 1;
+      if (st.row < N && st.col0 + h * kStatTile < V) {
+        const int64_t idx = (st.col0 / kStatTile + h) * N + st.row;
         tile_max[idx] = st.m;
         tile_sum[idx] = st.s;
       }
@@ -211,32 +286,45 @@ struct DlogitsEpi {
   T* dl;                // [N][ld], column 0 = local vocab row vc0
   float* grad_bias;     // [V] or nullptr
   const float* scale;   // fp16: {s, 1/s}, dl holds w / s; nullptr = unscaled (bf16)
-  const uint8_t* mask_src;  // keep + vc0 / 128: the chunk's columns of the [nRb][nVt] mask
+  const uint8_t* mask_src;  // keep + vc0 / 64: the chunk's columns of the [nRb][nVt] mask
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, stat tiles in the chunk
   int64_t N, V, v_offset, vc0, vc_end, ld;
+  // 1: every 64-column group of an active tile is written (the CTA-pair grad
+  // GEMMs read whole 256-row tiles); 0: only 128-column halves holding a kept
+  // group (the single-CTA grad_c reads 128-row tiles, grad_e kept groups).
+  int all_groups;
 
   struct State {
     int64_t row, tl, col0;
-    float g, L, s;  // g = d_nll / s
-    bool k0, k1;
+    float g, L, s;   // g = d_nll / s
+    uint32_t kmask;  // kept 64-column groups of the tile
+    int y0;          // first row of this warp's 32-row slab
   };
 
-  // The mask slice is read through `mk` (shared copy, row stride mld); the
-  // tile's two 128-column halves are the chunk's stat tiles 2 nb and 2 nb + 1.
+  // The tile's four 64-column groups are the chunk's stat tiles 4 nb .. 4 nb + 3.
   static constexpr bool kMask = true;
-  __device__ __forceinline__ bool tile_active(const uint8_t* mk, int64_t mld, int mb, int nb) const {
-    if (mb >= mask_rows) return false;
-    const uint8_t* kr = mk + (int64_t)mb * mld;
-    return kr[2 * nb] || (2 * nb + 1 < mask_cols && kr[2 * nb + 1]);
+  // Kept 64-column groups of the tile (bit g = chunk stat tile 4 nb + g).
+  __device__ __forceinline__ uint32_t group_mask(const MaskView& mk, int mb, int nb) const {
+    uint32_t m = 0;
+    if (mb < mask_rows) {
+#pragma unroll
+      for (int g = 0; g < BN / kStatTile; ++g) {
+        const int t = (BN / kStatTile) * nb + g;
+        if (t < mask_cols && mk.get(mb, t)) m |= 1u << g;
+      }
+    }
+    return m;
   }
-  __device__ __forceinline__ bool kb_active(const uint8_t*, int64_t, int, int, int) const { return true; }
+  __device__ __forceinline__ bool tile_active(const MaskView& mk, int mb, int nb) const {
+    return group_mask(mk, mb, nb) != 0;
+  }
+  __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
 
   // Rejected tiles are not written: the grad GEMMs skip exactly those blocks.
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
-  __device__ __forceinline__ void begin(State& st, const uint8_t* mk, int64_t mld, int mb, int nb,
-                                        int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView& mk, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = vc0 + (int64_t)nb * BN;  // local vocab id of the tile's column 0
     const bool ok = st.row < N;
@@ -244,14 +332,13 @@ struct DlogitsEpi {
     st.g = ok ? d_nll[st.row] * (scale ? scale[1] : 1.f) : 0.f;
     st.L = ok ? lse[st.row] : 0.f;
     st.tl = ok ? (int64_t)targets[st.row] - v_offset : -1;
-    const uint8_t* kr = mk + (int64_t)mb * mld;
-    st.k0 = mb < mask_rows && kr[2 * nb] != 0;
-    st.k1 = mb < mask_rows && (2 * nb + 1 < mask_cols) && kr[2 * nb + 1] != 0;
+    st.kmask = group_mask(mk, mb, nb);
+    st.y0 = (int)(st.row - (threadIdx.x & 31));
   }
 
-  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
     const int64_t cb = st.col0 + c * 32;
-    const bool kept = (c < 4) ? st.k0 : st.k1;
+    const bool kept = (st.kmask >> (c >> 1)) & 1u;
     float b[32];
     if constexpr (!std::is_void<TB>::value) {
       load_bias32<TB>(bias, cb, vc_end, b);
@@ -269,11 +356,7 @@ struct DlogitsEpi {
       }
       v[j] = w;
     }
-    if (st.row < N) {
-      T* dst = dl + st.row * ld + (cb - vc0);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) store8<T>(dst + g * 8, v + g * 8);
-    }
+    if (all_groups || ((st.kmask >> (2 * (c >> 2))) & 3u)) sg.store16<T>(v, (int)(cb - vc0), st.y0);
     if (grad_bias != nullptr) {
       const int lane = threadIdx.x & 31;
       const float colsum = warp_transpose_sum32(v);
@@ -293,7 +376,7 @@ struct GradEEpi {
   float* acc;   // [N, D] fp32 accumulator
   T* out;       // [N, D] final output (write_out)
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
-  const uint8_t* mask_src;  // keep + vc0 / 128: the chunk's columns of the [nRb][nVt] mask
+  const uint8_t* mask_src;  // keep + vc0 / 64: the chunk's columns of the [nRb][nVt] mask
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, stat tiles in the chunk
   int64_t N, D;
@@ -302,45 +385,48 @@ struct GradEEpi {
   struct State {
     int64_t row, col0;
     float s;
+    int y0;  // first row of this warp's 32-row slab
   };
-  // The mask slice [row block][stat tile of the chunk] is read through `mk`
-  // (shared copy, row stride mld).  K runs over the chunk's vocabulary rows:
-  // K-block kb (64 rows) lies in the chunk's stat tile kb / 2.
+  // K runs over the chunk's vocabulary rows: K-block kb (64 rows) is the
+  // chunk's stat tile kb.
   static constexpr bool kMask = true;
-  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
-  __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
-    return mb < mask_rows && mk[(int64_t)mb * mld + (kb >> 1)] != 0;
+  __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
+    return mb < mask_rows && kb < mask_cols && mk.get(mb, kb);
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
-  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
     st.s = scale ? scale[0] : 1.f;
+    st.y0 = (int)(st.row - (threadIdx.x & 31));
   }
-  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
-    if (st.row >= N) return;
+  // Not the last chunk: the tile goes to the fp32 accumulator by TMA (a store
+  // for the first chunk, a reduce-add after it).  Last chunk: accumulator +
+  // tile -> T output.  The stager's tensor map is acc (fp32) or out (T).
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
     const int64_t cb = st.col0 + c * 32;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int64_t col = cb + g * 8;
-      if (col >= D) break;
-      float* a = acc + st.row * D + col;
-      float o[8];
+    for (int j = 0; j < 32; ++j) v[j] *= st.s;
+    if (!write_out) {
+      sg.store_f32(v, (int)cb, st.y0, accumulate != 0);
+      return;
+    }
+    if (accumulate && st.row < N) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i] * st.s;
-      if (accumulate) {
-        const float4 x0 = *reinterpret_cast<const float4*>(a);
-        const float4 x1 = *reinterpret_cast<const float4*>(a + 4);
-        o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
-        o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
-      }
-      if (write_out) {
-        store8<T>(out + st.row * D + col, o);
-      } else {
-        *reinterpret_cast<float4*>(a) = make_float4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<float4*>(a + 4) = make_float4(o[4], o[5], o[6], o[7]);
+      for (int g = 0; g < 4; ++g) {
+        const int64_t col = cb + g * 8;
+        if (col < D) {
+          const float* a = acc + st.row * D + col;
+          const float4 x0 = *reinterpret_cast<const float4*>(a);
+          const float4 x1 = *reinterpret_cast<const float4*>(a + 4);
+          float* o = v + g * 8;
+          o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
+          o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
+        }
       }
     }
+    sg.store16<T>(v, (int)cb, st.y0);
   }
   __device__ __forceinline__ void end(State&) const {}
 };
@@ -353,7 +439,7 @@ template <typename T>
 struct GradCEpi {
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
-  const uint8_t* mask_src;  // keep + vc0 / 128
+  const uint8_t* mask_src;  // keep + vc0 / 64
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, stat tiles in the chunk
   int64_t rows, D;
@@ -361,31 +447,27 @@ struct GradCEpi {
   struct State {
     int64_t row, col0;
     float s;
+    int y0;  // first row of this warp's 32-row slab
   };
-  // M tile mb is the chunk's stat tile mb; K-block kb (64 rows) lies in row block kb / 2.
+  // M tile mb covers the chunk's stat tiles 2 mb and 2 mb + 1; K-block kb (64
+  // rows) lies in row block kb / 2.
   static constexpr bool kMask = true;
-  __device__ __forceinline__ bool tile_active(const uint8_t*, int64_t, int, int) const { return true; }
-  __device__ __forceinline__ bool kb_active(const uint8_t* mk, int64_t mld, int mb, int, int kb) const {
-    return mb < mask_cols && mk[(int64_t)(kb >> 1) * mld + mb] != 0;
+  __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
+    const int t = 2 * mb;
+    return (t < mask_cols && mk.get(kb >> 1, t)) || (t + 1 < mask_cols && mk.get(kb >> 1, t + 1));
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
-  __device__ __forceinline__ void begin(State& st, const uint8_t*, int64_t, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
     st.s = scale ? scale[0] : 1.f;
+    st.y0 = (int)(st.row - (threadIdx.x & 31));
   }
-  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32]) const {
-    if (st.row >= rows) return;
-    const int64_t cb = st.col0 + c * 32;
+  __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int64_t col = cb + g * 8;
-      if (col >= D) break;
-      float o[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[g * 8 + i] * st.s;
-      store8<T>(out + st.row * D + col, o);
-    }
+    for (int j = 0; j < 32; ++j) v[j] *= st.s;
+    sg.store16<T>(v, (int)(st.col0 + c * 32), st.y0);
   }
   __device__ __forceinline__ void end(State&) const {}
 };
@@ -397,13 +479,15 @@ struct GradCEpi {
 template <bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const Sched sched, const Epi epi, const uint32_t idesc) {
+               const __grid_constant__ CUtensorMap tmC, const Sched sched, const Epi epi,
+               const uint32_t idesc) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sOut = sB + STAGES * B_BYTES;   // epilogue staging (1 KB aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -435,20 +519,25 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     prefetch_tmap(&tmB);
   }
   // Filter-mask slice: copied to shared memory when it fits, else read in place.
-  const uint8_t* mk = nullptr;
-  int64_t mld = 0;
+  MaskView mk{nullptr, nullptr, 0, 0};
   if constexpr (Epi::kMask) {
     const int rows = epi.mask_rows, cols = epi.mask_cols;
-    if ((int64_t)rows * cols <= SMASK_BYTES) {
+    const int wpr = (cols + 31) / 32;
+    if ((int64_t)rows * wpr * 4 <= SMASK_BYTES) {
+      uint32_t* sb = reinterpret_cast<uint32_t*>(smask);
       for (int rr = warp; rr < rows; rr += kThreads / 32) {
         const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
-        for (int cc = lane; cc < cols; cc += 32) smask[rr * cols + cc] = __ldg(src + cc);
+        for (int c0 = 0; c0 < cols; c0 += 32) {
+          const int cc = c0 + lane;
+          const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
+          if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
+        }
       }
-      mk = smask;
-      mld = cols;
+      mk.bits = sb;
+      mk.wpr = wpr;
     } else {
-      mk = epi.mask_src;
-      mld = epi.mask_ld;
+      mk.bytes = epi.mask_src;
+      mk.ld = epi.mask_ld;
     }
   }
   if (warp == 1) {
@@ -478,10 +567,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (i + 1) * (int)gridDim.x;
         int mb, nb;
         sched.coords(tile, mb, nb);
-        if (!epi.tile_active(mk, mld, mb, nb)) continue;
+        if (!epi.tile_active(mk, mb, nb)) continue;
         bool ok = true;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!epi.kb_active(mk, mld, mb, nb, kb)) continue;
+          if (!epi.kb_active(mk, mb, nb, kb)) continue;
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
           uint8_t* a = sA + stage * A_BYTES;
@@ -539,14 +628,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (tile < 0) break;
         int mb, nb;
         sched.coords(tile, mb, nb);
-        if (!epi.tile_active(mk, mld, mb, nb)) continue;
+        if (!epi.tile_active(mk, mb, nb)) continue;
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         uint32_t issued = 0;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!epi.kb_active(mk, mld, mb, nb, kb)) continue;
+          if (!epi.kb_active(mk, mb, nb, kb)) continue;
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
@@ -572,6 +661,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
+    Stager sg{&tmC, sOut + q * 4096, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int i = 0;; ++i) {
@@ -582,16 +672,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (tile < 0) break;
       int mb, nb;
       sched.coords(tile, mb, nb);
-      if (!epi.tile_active(mk, mld, mb, nb)) {
+      if (!epi.tile_active(mk, mb, nb)) {
         epi.inactive_tile(mb, nb, r);
         continue;
       }
       if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
       tc_fence_after();
       bool any_kb = !Epi::kMask;
-      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = epi.kb_active(mk, mld, mb, nb, kb);
+      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = epi.kb_active(mk, mb, nb, kb);
       typename Epi::State st;
-      epi.begin(st, mk, mld, mb, nb, r);
+      epi.begin(st, mk, mb, nb, r);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -603,7 +693,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        epi.chunk(st, c, v);
+        epi.chunk(st, c, v, sg);
       }
       epi.end(st);
       __syncwarp();
@@ -612,6 +702,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    sg.drain();  // output boxes written before the kernel ends
   }
 
   tc_fence_before();
@@ -642,18 +733,20 @@ constexpr int STAGES2 = 6;
 constexpr uint32_t A2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 rows of A
 constexpr uint32_t B2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 columns of B
 constexpr uint32_t STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr size_t SMEM2_BYTES = 1024 + STAGES2 * (size_t)STAGE2_BYTES + 256 + SMASK_BYTES;
+constexpr size_t SMEM2_BYTES = 1024 + STAGES2 * (size_t)STAGE2_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
 
 template <bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const Sched sched, const Epi epi, const uint32_t idesc) {
+                const __grid_constant__ CUtensorMap tmC, const Sched sched, const Epi epi,
+                const uint32_t idesc) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES2 * A2_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES2 * B2_BYTES);
+  uint8_t* sOut = sB + STAGES2 * B2_BYTES;   // epilogue staging (1 KB aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_STAGE_BYTES);
   uint64_t* empty = full + STAGES2;
   uint64_t* tfull = empty + STAGES2;
   uint64_t* tempty = tfull + 2;
@@ -687,20 +780,25 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  const uint8_t* mk = nullptr;
-  int64_t mld = 0;
+  MaskView mk{nullptr, nullptr, 0, 0};
   if constexpr (Epi::kMask) {
     const int rows = epi.mask_rows, cols = epi.mask_cols;
-    if ((int64_t)rows * cols <= SMASK_BYTES) {
+    const int wpr = (cols + 31) / 32;
+    if ((int64_t)rows * wpr * 4 <= SMASK_BYTES) {
+      uint32_t* sb = reinterpret_cast<uint32_t*>(smask);
       for (int rr = warp; rr < rows; rr += kThreads / 32) {
         const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
-        for (int cc = lane; cc < cols; cc += 32) smask[rr * cols + cc] = __ldg(src + cc);
+        for (int c0 = 0; c0 < cols; c0 += 32) {
+          const int cc = c0 + lane;
+          const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
+          if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
+        }
       }
-      mk = smask;
-      mld = cols;
+      mk.bits = sb;
+      mk.wpr = wpr;
     } else {
-      mk = epi.mask_src;
-      mld = epi.mask_ld;
+      mk.bytes = epi.mask_src;
+      mk.ld = epi.mask_ld;
     }
   }
   if (warp == 1) {
@@ -715,10 +813,10 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
   // A pair tile is active / has an active K-block when either CTA's half does.
   auto tile_on = [&](int mb, int nb) {
-    return epi.tile_active(mk, mld, 2 * mb, nb) || epi.tile_active(mk, mld, 2 * mb + 1, nb);
+    return epi.tile_active(mk, 2 * mb, nb) || epi.tile_active(mk, 2 * mb + 1, nb);
   };
   auto kb_on = [&](int mb, int nb, int kb) {
-    return epi.kb_active(mk, mld, 2 * mb, nb, kb) || epi.kb_active(mk, mld, 2 * mb + 1, nb, kb);
+    return epi.kb_active(mk, 2 * mb, nb, kb) || epi.kb_active(mk, 2 * mb + 1, nb, kb);
   };
   const uint32_t full_leader = mapa_shared(smem_u32(full), 0);   // + 8 * stage
   const uint32_t rempty_leader = mapa_shared(smem_u32(rempty), 0);
@@ -855,6 +953,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    Stager sg{&tmC, sOut + q * 4096, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int i = 0;; ++i) {
@@ -883,7 +982,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       bool any_kb = !Epi::kMask;
       for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = kb_on(mb, nb, kb);
       typename Epi::State st;
-      epi.begin(st, mk, mld, vmb, nb, r);
+      epi.begin(st, mk, vmb, nb, r);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -895,7 +994,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        epi.chunk(st, c, v);
+        epi.chunk(st, c, v, sg);
       }
       epi.end(st);
       __syncwarp();
@@ -908,6 +1007,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    sg.drain();  // output boxes written before the kernel ends
   }
 
   tc_fence_before();
@@ -1001,9 +1101,28 @@ bool make_tmap_mn(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, i
   return make_tmap(tm, base, bf16, inner, outer, ld, 64, BK);
 }
 
+// Epilogue output map: row-major [outer][inner] of `dtype` (CCE_F32 / F16 /
+// BF16), row stride `ld` elements, written in (box_inner x 32) boxes of 64
+// bytes per row with the 64-byte swizzle the Stager lays out.
+bool make_tmap_out(CUtensorMap* tm, const void* base, int dtype, int64_t inner, int64_t outer, int64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const int es = dtype == CCE_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = dtype == CCE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == CCE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(64 / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(tm, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <bool A_MN, bool B_MN, class Epi>
-cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sched& s, const Epi& epi,
-                        bool bf16, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                        const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<A_MN, B_MN, Epi>;
   static std::atomic<int> attr_done[64];
   int dev = 0;
@@ -1018,13 +1137,13 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sc
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, s, epi, idesc);
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmC, s, epi, idesc);
   return launched();
 }
 
 template <bool A_MN, bool B_MN, class Epi>
-cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const Sched& s, const Epi& epi,
-                         bool bf16, cudaStream_t stream) {
+cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                         const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm2_kernel<A_MN, B_MN, Epi>;
   static std::atomic<int> attr_done[64];
   int dev = 0;
@@ -1052,7 +1171,7 @@ cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const S
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, s, epi, idesc);
+  err = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, s, epi, idesc);
   if (err != cudaSuccess) return err;
   return launched();
 }
@@ -1097,8 +1216,9 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            nullptr, raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
-  if (pair) return launch_gemm2<false, false>(tmA, tmB, sc, epi, bf16, s);
-  return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
+  const CUtensorMap tmC{};  // the forward epilogue writes no tiles
+  if (pair) return launch_gemm2<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 template <typename T, typename TB>
@@ -1115,9 +1235,11 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
-                        a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
-  if (pair) return launch_gemm2<false, false>(tmA, tmB, sc, epi, bf16, s);
-  return launch_gemm<false, false>(tmA, tmB, sc, epi, bf16, s);
+                        a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld, pair ? 1 : 0};
+  CUtensorMap tmC;
+  if (!make_tmap_out(&tmC, a.dlogits, a.dtype, a.vc_len, a.N, a.vc_ld)) return cudaErrorInvalidValue;
+  if (pair) return launch_gemm2<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace
@@ -1170,8 +1292,12 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* grad_e_acc, bool accumul
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                   a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
-  if (pair) return launch_gemm2<false, true>(tmA, tmB, sc, epi, bf16, s);
-  return launch_gemm<false, true>(tmA, tmB, sc, epi, bf16, s);
+  CUtensorMap tmC;
+  const bool okC = write_out ? make_tmap_out(&tmC, grad_e_out, a.dtype, a.D, a.N, a.D)
+                             : make_tmap_out(&tmC, grad_e_acc, CCE_F32, a.D, a.N, a.D);
+  if (!okC) return cudaErrorInvalidValue;
+  if (pair) return launch_gemm2<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 template <typename T>
@@ -1188,8 +1314,11 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
                   a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                   (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                   a.vc_len, a.D};
-  if (pair) return launch_gemm2<true, true>(tmA, tmB, sc, epi, bf16, s);
-  return launch_gemm<true, true>(tmA, tmB, sc, epi, bf16, s);
+  CUtensorMap tmC;
+  if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
+    return cudaErrorInvalidValue;
+  if (pair) return launch_gemm2<true, true>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<true, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace

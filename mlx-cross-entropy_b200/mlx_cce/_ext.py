@@ -35,7 +35,7 @@ CCE_ERR_WORKSPACE = -6
 CCE_ERR_ARG = -7
 
 CCE_F32, CCE_F16, CCE_BF16 = 0, 1, 2
-CCE_STAT_TILE = 128
+CCE_STAT_TILE = 64
 
 CCE_NEED_DE = 1
 CCE_NEED_DC = 2
@@ -321,8 +321,8 @@ def cce_forward_raw(e, c, targets, bias=None, *, stream=None):
     """Mirror of ``cce_forward_raw`` (csrc/bindings.cpp:58-69, cce.cpp:123-145).
 
     Returns ``[tile_max_flat, tile_sum_exp_flat, neg_target_logit, lse]`` like
-    the reference, except that the tile statistics cover 128-column tiles in
-    tile-major order (``[ceil(V/128) * N]``) and ``tile_sum_exp`` is not kept
+    the reference, except that the tile statistics cover 64-column tiles in
+    tile-major order (``[ceil(V/64) * N]``) and ``tile_sum_exp`` is not kept
     (it is folded into ``lse`` on the device), so an empty tensor stands in.
     """
     tile_max, lse, tgt = forward(e, c, _as_i32_targets(targets), bias, stream=stream)

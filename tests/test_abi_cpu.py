@@ -31,16 +31,16 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_tile_count():
     assert _ext.version() == 100
-    assert _ext.num_stat_tiles(128256) == 1002
-    assert _ext.num_stat_tiles(128) == 1
-    assert _ext.num_stat_tiles(129) == 2
+    assert _ext.num_stat_tiles(128256) == 2004
+    assert _ext.num_stat_tiles(64) == 1
+    assert _ext.num_stat_tiles(65) == 2
     assert _ext.num_stat_tiles(0) == 0
 
 
 def test_workspace_sizes():
     lib = _ext.lib
     f = lib.cce_forward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16)
-    assert f >= 1002 * 4096 * 4 and f % 256 == 0
+    assert f >= 2004 * 4096 * 4 and f % 256 == 0
     flags = _ext.CCE_NEED_DE | _ext.CCE_NEED_DC
     b = lib.cce_backward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16, flags)
     # mask + a bounded dlogits chunk (never [N, V]) + the fp32 grad_e accumulator

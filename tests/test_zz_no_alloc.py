@@ -3,7 +3,7 @@
 Some hosts can hand the loss its inputs and outputs but have no device
 allocator to offer for a workspace (a plugin or FFI slot with a fixed memory
 contract, or a runtime that forbids allocation while it executes).  For them
-cce_forward_noalloc keeps its scratch in a static 16 MiB array inside the
+cce_forward_noalloc keeps its scratch in a static 32 MiB array inside the
 library.  This test calls it through the C ABI twice in a row -- the second
 call smaller than the first, so the shared array still holds the first call's
 partials -- and checks each result against cce_forward with a caller-owned
@@ -66,7 +66,7 @@ def test_noalloc_forward_matches_workspace_forward_twice():
 
 
 def test_noalloc_rejects_calls_beyond_its_capacity():
-    # ceil(V / 128) * N above 4194304 partials: refused before any GPU work
+    # ceil(V / 64) * N above 8388608 partials: refused before any GPU work
     rc = _ext.lib.cce_forward_noalloc(None, None, None, 0, None, 4186, 4096, 128256, 0,
                                       _ext.CCE_BF16, None, None, None, None)
     assert rc == _ext.CCE_ERR_WORKSPACE
