@@ -222,8 +222,11 @@ struct FwdEpi {
 
   static constexpr bool kMask = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
   __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  template <class S>
+  __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
 
   __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
@@ -319,6 +322,12 @@ struct DlogitsEpi {
   __device__ __forceinline__ bool tile_active(const MaskView& mk, int mb, int nb) const {
     return group_mask(mk, mb, nb) != 0;
   }
+  // 64-column groups the MMA computes: only the kept ones (the epilogue never
+  // reads the accumulator columns of the others).
+  __device__ __forceinline__ uint32_t col_mask(const MaskView& mk, int mb, int nb) const {
+    return all_groups ? 0xFu : group_mask(mk, mb, nb);
+  }
+  __device__ __forceinline__ bool chunk_live(const State& st, int c) const { return (st.kmask >> (c >> 1)) & 1u; }
   __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
 
   // Rejected tiles are not written: the grad GEMMs skip exactly those blocks.
@@ -391,10 +400,13 @@ struct GradEEpi {
   // chunk's stat tile kb.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
   __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
     return mb < mask_rows && kb < mask_cols && mk.get(mb, kb);
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  template <class S>
+  __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
   __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
@@ -453,11 +465,14 @@ struct GradCEpi {
   // rows) lies in row block kb / 2.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
   __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
     const int t = 2 * mb;
     return (t < mask_cols && mk.get(kb >> 1, t)) || (t + 1 < mask_cols && mk.get(kb >> 1, t + 1));
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  template <class S>
+  __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
   __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
@@ -632,6 +647,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        // The tile's 64-column groups to compute: when they form one run of
+        // consecutive groups (j0, n0), one MMA of N = 64 n0 columns at B rows
+        // 64 j0 (K-major B: 8 KB per 64 rows); else the whole tile.  (Two
+        // runs as two MMAs re-read A from shared memory and measured slower.)
+        uint32_t j0 = 0, n0 = BN / 64;
+        if constexpr (!B_MN) {
+          const uint32_t cm = epi.col_mask(mk, mb, nb);
+          if (cm != 0xFu) {
+            const uint32_t j = __ffs(cm) - 1;
+            const uint32_t n = __ffs(~(cm >> j)) - 1;
+            if ((cm >> (j + n)) == 0u) {
+              j0 = j;
+              n0 = n;
+            }
+          }
+        }
+        const uint32_t idesc0 = idesc_with_n(idesc, 64 * n0);
         bool ok = true;
         uint32_t issued = 0;
         for (int kb = 0; kb < sched.num_kb; ++kb) {
@@ -641,8 +673,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
           const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16(d_tmem, ad + k * a_kstep, bd + k * b_kstep, idesc, (issued | (uint32_t)k) != 0 ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accf = (issued | (uint32_t)k) != 0 ? 1u : 0u;
+            mma_f16(d_tmem + 64 * j0, ad + k * a_kstep, bd + ((8192u * j0) >> 4) + k * b_kstep, idesc0, accf);
+          }
           ++issued;
           mma_commit(empty + stage);
           if (++stage == STAGES) {
@@ -687,7 +721,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         __syncwarp();
-        if (any_kb) {
+        if (any_kb && epi.chunk_live(st, c)) {
           tmem_ld32(tbase + c * 32, v);
         } else {
 #pragma unroll
@@ -988,7 +1022,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         __syncwarp();
-        if (any_kb) {
+        if (any_kb && epi.chunk_live(st, c)) {
           tmem_ld32(tbase + c * 32, v);
         } else {
 #pragma unroll

@@ -319,5 +319,10 @@ __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool bf16, bool 
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// The same descriptor with the N field (bits 17-22, N >> 3) replaced.
+__host__ __device__ constexpr uint32_t idesc_with_n(uint32_t idesc, int N) {
+  return (idesc & ~(0x3Fu << 17)) | (static_cast<uint32_t>(N >> 3) << 17);
+}
+
 }  // namespace tc
 }  // namespace cce
