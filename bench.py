@@ -362,7 +362,7 @@ def run_ours(args, rank, world, local_rank):
                          "frac": fwd_tflops / peak,
                          "peak_kind": f"{src} bf16 {'sustained' if long_run else 'burst'}",
                          "traffic": traffic,
-                         "algorithmic_bytes": 2.0 * (N * D + vl * D) + 8.0 * N * (-(-vl // 64))},
+                         "algorithmic_bytes": 2.0 * (N * D + vl * D) + 8.0 * N * (-(-vl // 32))},
             "e2e": {"value": N * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # library kernels per K steps (counted in the eager region; a graph

@@ -56,7 +56,7 @@ extern "C" {
 
 /* Vocabulary columns summarised by one tile statistic.  tile_max is laid out
  * [ceil(V / CCE_STAT_TILE)][N] (tile-major, rows contiguous). */
-#define CCE_STAT_TILE 64
+#define CCE_STAT_TILE 32
 
 /* backward flags */
 #define CCE_NEED_DE     1   /* write grad_e                                       */
@@ -105,8 +105,8 @@ CCE_API size_t cce_forward_workspace_bytes(int64_t N, int64_t D, int64_t V, int 
  *   e        [N, D]   dtype          c [V, D] dtype
  *   bias     [V]      bias_dtype or NULL
  *   targets  [N]      int32 sanitised global ids
- *   tile_max [ceil(V/64)][N] fp32 out: max logit (+bias) of each row over
- *            each 64-column vocabulary tile (the backward's filter input)
+ *   tile_max [ceil(V/32)][N] fp32 out: max logit (+bias) of each row over
+ *            each 32-column vocabulary tile (the backward's filter input)
  *   lse      [N] fp32 out: log-sum-exp over this call's V columns
  *   tgt      [N] fp32 out: logit (+bias) of the row's target when the target
  *            lies in [v_offset, v_offset + V), else 0
@@ -129,7 +129,7 @@ CCE_API int cce_forward(const void* e, const void* c, const void* bias, int bias
  * that can pass inputs and outputs but own no allocator: a plugin or FFI slot
  * with a fixed memory contract, or a host that forbids allocation while it
  * runs.  It calls no cudaMalloc / cudaFree.
- *   - limit: ceil(V / 64) * N <= 8388608 (e.g. V = 128256, N <= 4185);
+ *   - limit: 2 * ceil(V / 128) * N <= 8388608 (e.g. V = 128256, N <= 4185);
  *     larger calls return CCE_ERR_WORKSPACE and do nothing.
  *   - the first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
@@ -172,12 +172,12 @@ CCE_API size_t cce_backward_workspace_bytes(int64_t N, int64_t D, int64_t V, int
  *
  *   lse       [N] fp32: GLOBAL log-sum-exp (after any cross-shard combine)
  *   d_nll     [N] fp32: cotangent of each row's NLL (0 for ignored rows)
- *   tile_max  [ceil(V/64)][N] fp32 from cce_forward
+ *   tile_max  [ceil(V/32)][N] fp32 from cce_forward
  *   grad_e    [N, D] e's dtype, or fp32 with CCE_DE_F32 (overwritten)
  *   grad_c    [V, D] c's dtype (overwritten; NULL unless CCE_NEED_DC)
  *   grad_bias [V] fp32 (overwritten; NULL unless CCE_NEED_DBIAS)
  *   skip_stats device int64[2] (nullable): accumulates (skipped, total)
- *            (128-row x 64-column) blocks of this call
+ *            (128-row x 32-column) blocks of this call
  *   filter_log_eps: a block whose every row has tile_max - lse below it and
  *            holds no target is skipped (CCE_FILTER_LOG_EPS = the reference's).
  */

@@ -14,7 +14,7 @@ namespace cce {
 
 namespace {
 
-constexpr int kCombRows = 32;    // rows per block (threadIdx.x)
+constexpr int kCombRows = 32;    // rows per block (threadIdx.x): a warp reads 128 contiguous bytes
 constexpr int kCombSlices = 32;  // partial slices per row (threadIdx.y)
 
 // Fold (mp, sp) into the running (m, s): s * 2^(m - M) + sp * 2^(mp - M), M = max.
@@ -29,9 +29,9 @@ __global__ void __launch_bounds__(kCombRows * kCombSlices)
 lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__ part_sum,
                    const float* __restrict__ part_tgt, int64_t P, int64_t N, int64_t ld,
                    float* __restrict__ lse, float* __restrict__ tgt, float* __restrict__ nll) {
-  __shared__ float sm[kCombSlices][kCombRows + 1];
-  __shared__ float ss[kCombSlices][kCombRows + 1];
-  __shared__ float st[kCombSlices][kCombRows + 1];
+  __shared__ float sm[kCombSlices][kCombRows];
+  __shared__ float ss[kCombSlices][kCombRows];
+  __shared__ float st[kCombSlices][kCombRows];
   const int64_t row = (int64_t)blockIdx.x * kCombRows + threadIdx.x;
   float m = -INFINITY, s = 0.f, t = 0.f;
   if (row < N) {
@@ -65,48 +65,98 @@ lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__
   ss[threadIdx.y][threadIdx.x] = s;
   st[threadIdx.y][threadIdx.x] = t;
   __syncthreads();
-  if (threadIdx.y == 0 && row < N) {
-    float M = -INFINITY, S = 0.f, T = 0.f;
-    for (int i = 0; i < kCombSlices; ++i) {
-      fold(M, S, sm[i][threadIdx.x], ss[i][threadIdx.x]);
-      T += st[i][threadIdx.x];
+  // tree fold over the slices
+  for (int h = kCombSlices / 2; h >= 1; h >>= 1) {
+    if (threadIdx.y < h) {
+      float M = sm[threadIdx.y][threadIdx.x], S = ss[threadIdx.y][threadIdx.x];
+      fold(M, S, sm[threadIdx.y + h][threadIdx.x], ss[threadIdx.y + h][threadIdx.x]);
+      sm[threadIdx.y][threadIdx.x] = M;
+      ss[threadIdx.y][threadIdx.x] = S;
+      st[threadIdx.y][threadIdx.x] += st[threadIdx.y + h][threadIdx.x];
     }
-    const float L = M + logf(S);
+    __syncthreads();
+  }
+  if (threadIdx.y == 0 && row < N) {
+    const float L = sm[0][threadIdx.x] + logf(ss[0][threadIdx.x]);
+    const float T = st[0][threadIdx.x];
     lse[row] = L;
     if (tgt) tgt[row] = T;
     if (nll) nll[row] = L - T;
   }
 }
 
-__global__ void __launch_bounds__(kRowBlock)
+// One block = one 128-row block x kMaskTiles statistics tiles; each warp
+// decides kMaskTiles / 8 tiles, its lane l covering rows l, l + 32, l + 64 and
+// l + 96 (coalesced tile_max loads, per-row inputs read once).  Besides the
+// byte mask keep[row block][tile], the block ORs its decisions per 128-column
+// tile into the transposed bit table keep_t[128-column tile][row block bits]
+// (zeroed by the caller; nullable).  The skip counters take one atomic pair
+// per block.
+constexpr int kMaskTiles = 32;
+constexpr int kMaskWarps = 8;
+constexpr int kTilesPer128 = 128 / kStatTile;
+static_assert(kMaskTiles % kTilesPer128 == 0, "whole 128-column tiles per block");
+
+__global__ void __launch_bounds__(kMaskWarps * 32)
 block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ lse,
                   const int32_t* __restrict__ targets, const float* __restrict__ d_nll, int64_t N,
                   int64_t V, int64_t v_offset, float log_eps, int no_filter, uint8_t* __restrict__ keep,
+                  uint32_t* __restrict__ keep_t, int64_t keep_t_ld,
                   unsigned long long* __restrict__ skip_stats) {
-  const int64_t j = blockIdx.x;   // vocabulary tile
-  const int64_t i = blockIdx.y;   // row block
-  const int64_t row = i * kRowBlock + threadIdx.x;
-  const int64_t nVt = gridDim.x;
-  int k = 0;
-  if (row < N) {
-    const float g = d_nll[row];
-    if (g != 0.f) {  // rows with a zero cotangent contribute nothing
-      if (no_filter) {
-        k = 1;
-      } else {
-        const int64_t tl = (int64_t)targets[row] - v_offset;
-        const bool hit = tl >= j * kStatTile && tl < (j + 1) * kStatTile && tl < V;
-        k = hit || (tile_max[j * N + row] - lse[row] >= log_eps);
+  __shared__ uint32_t any128[kMaskTiles / kTilesPer128];
+  if (threadIdx.x < kMaskTiles / kTilesPer128) any128[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t nVt = ceil_div(V, kStatTile);
+  const int64_t i = blockIdx.y;  // row block
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kRowsPerLane = kRowBlock / 32;
+  float L[kRowsPerLane];
+  int64_t tl[kRowsPerLane];
+  bool live[kRowsPerLane];
+  const float* tm[kRowsPerLane];
+#pragma unroll
+  for (int u = 0; u < kRowsPerLane; ++u) {
+    const int64_t row = i * kRowBlock + lane + 32 * u;
+    live[u] = row < N && d_nll[row] != 0.f;  // rows with a zero cotangent contribute nothing
+    L[u] = live[u] ? lse[row] : 0.f;
+    tl[u] = live[u] ? (int64_t)targets[row] - v_offset : -1;
+    tm[u] = tile_max + (live[u] ? row : 0);
+  }
+  int skipped = 0, total = 0;
+  for (int w = warp; w < kMaskTiles; w += kMaskWarps) {
+    const int64_t j = (int64_t)blockIdx.x * kMaskTiles + w;  // vocabulary tile
+    if (j >= nVt) break;
+    bool k = false;
+#pragma unroll
+    for (int u = 0; u < kRowsPerLane; ++u) {
+      if (live[u]) {
+        const bool hit = tl[u] >= j * kStatTile && tl[u] < (j + 1) * kStatTile && tl[u] < V;
+        k = k || no_filter || hit || (tm[u][j * N] - L[u] >= log_eps);
       }
     }
-  }
-  k = __syncthreads_or(k);
-  if (threadIdx.x == 0) {
-    keep[i * nVt + j] = (uint8_t)k;
-    if (skip_stats) {
-      atomicAdd(&skip_stats[1], 1ull);
-      if (!k) atomicAdd(&skip_stats[0], 1ull);
+    k = __any_sync(0xffffffffu, k);
+    if (lane == 0) {
+      keep[i * nVt + j] = (uint8_t)k;
+      if (k) any128[w / kTilesPer128] = 1u;  // benign race: every writer stores 1
     }
+    ++total;
+    skipped += k ? 0 : 1;
+  }
+  __shared__ int cnt[2];
+  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0;
+  __syncthreads();
+  if (skip_stats && lane == 0 && total) {
+    atomicAdd(&cnt[0], skipped);
+    atomicAdd(&cnt[1], total);
+  }
+  if (keep_t && threadIdx.x < kMaskTiles / kTilesPer128 && any128[threadIdx.x]) {
+    const int64_t m = (int64_t)blockIdx.x * (kMaskTiles / kTilesPer128) + threadIdx.x;  // 128-column tile
+    atomicOr(&keep_t[m * keep_t_ld + (i >> 5)], 1u << (i & 31));
+  }
+  __syncthreads();
+  if (skip_stats && threadIdx.x == 0 && cnt[1]) {
+    atomicAdd(&skip_stats[0], (unsigned long long)cnt[0]);
+    atomicAdd(&skip_stats[1], (unsigned long long)cnt[1]);
   }
 }
 
@@ -115,6 +165,27 @@ __global__ void cast_f32_kernel(const float* __restrict__ src, T* __restrict__ d
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     dst[i] = from_f32<T>(src[i]);
+}
+
+// dst = a + b; four elements per thread step when n is a multiple of 4 (all
+// pointers are then 16-byte aligned by the caller's contract), else one.
+template <typename T>
+__global__ void sum2_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, T* __restrict__ dst,
+                                int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if ((n & 3) == 0) {
+    for (int64_t i = i0; i < n / 4; i += stride) {
+      const float4 x = reinterpret_cast<const float4*>(a)[i];
+      const float4 y = reinterpret_cast<const float4*>(b)[i];
+      dst[4 * i] = from_f32<T>(x.x + y.x);
+      dst[4 * i + 1] = from_f32<T>(x.y + y.y);
+      dst[4 * i + 2] = from_f32<T>(x.z + y.z);
+      dst[4 * i + 3] = from_f32<T>(x.w + y.w);
+    }
+  } else {
+    for (int64_t i = i0; i < n; i += stride) dst[i] = from_f32<T>(a[i] + b[i]);
+  }
 }
 
 __global__ void fill_f32_kernel(float* __restrict__ dst, float v, int64_t n) {
@@ -172,12 +243,12 @@ cudaError_t launch_lse_combine(const float* part_max, const float* part_sum, con
 
 cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int32_t* targets,
                               const float* d_nll, int64_t N, int64_t V, int64_t v_offset,
-                              float log_eps, bool no_filter, uint8_t* keep, int64_t* skip_stats,
-                              cudaStream_t stream) {
+                              float log_eps, bool no_filter, uint8_t* keep, uint32_t* keep_t,
+                              int64_t keep_t_ld, int64_t* skip_stats, cudaStream_t stream) {
   if (N == 0 || V == 0) return cudaSuccess;
-  dim3 grid((unsigned)ceil_div(V, kStatTile), (unsigned)ceil_div(N, kRowBlock));
-  block_mask_kernel<<<grid, kRowBlock, 0, stream>>>(tile_max, lse, targets, d_nll, N, V, v_offset,
-                                                    log_eps, no_filter ? 1 : 0, keep,
+  dim3 grid((unsigned)ceil_div(ceil_div(V, kStatTile), (int64_t)kMaskTiles), (unsigned)ceil_div(N, kRowBlock));
+  block_mask_kernel<<<grid, kMaskWarps * 32, 0, stream>>>(tile_max, lse, targets, d_nll, N, V, v_offset,
+                                                    log_eps, no_filter ? 1 : 0, keep, keep_t, keep_t_ld,
                                                     reinterpret_cast<unsigned long long*>(skip_stats));
   return launched();
 }
@@ -194,6 +265,26 @@ cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, c
       break;
     case CCE_BF16:
       cast_f32_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(src, (__nv_bfloat16*)dst, n);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return launched();
+}
+
+cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const int grid = grid_for((n & 3) == 0 ? n / 4 : n, threads);
+  switch (dtype) {
+    case CCE_F32:
+      sum2_f32_kernel<float><<<grid, threads, 0, stream>>>(a, b, (float*)dst, n);
+      break;
+    case CCE_F16:
+      sum2_f32_kernel<__half><<<grid, threads, 0, stream>>>(a, b, (__half*)dst, n);
+      break;
+    case CCE_BF16:
+      sum2_f32_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(a, b, (__nv_bfloat16*)dst, n);
       break;
     default:
       return cudaErrorInvalidValue;

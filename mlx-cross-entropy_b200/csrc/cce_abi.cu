@@ -87,6 +87,8 @@ struct BwdPlan {
   bool tc;
   int64_t vc;        // chunk rows (also the dlogits row stride)
   size_t keep_bytes, dl_bytes, acc_bytes, counter_bytes, scale_bytes;
+  int64_t keep_t_ld;     // words per row of the transposed table (tensor-core path)
+  size_t keep_t_bytes;
 };
 
 bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
@@ -106,8 +108,16 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   if (vc > vmax) vc = vmax;
   p.vc = vc;
   p.keep_bytes = align_up((size_t)cce::ceil_div(N, cce::kRowBlock) * (size_t)cce::ceil_div(V, cce::kStatTile));
+  // grad_c's view of the mask: per 128-column tile a bit per row block
+  p.keep_t_ld = tc ? cce::ceil_div(cce::ceil_div(N, cce::kRowBlock), 32) : 0;
+  p.keep_t_bytes = tc ? align_up((size_t)cce::ceil_div(V, 128) * (size_t)p.keep_t_ld * 4) : 0;
   p.dl_bytes = align_up((size_t)N * (size_t)vc * (size_t)elt);
-  p.acc_bytes = ((flags & CCE_NEED_DE) && !(flags & CCE_DE_F32)) ? align_up((size_t)N * (size_t)D * 4) : 0;
+  // grad_e accumulators: the tensor-core path keeps two fp32 slabs [2][N][D]
+  // (the two K halves of every chunk's grad_e GEMM), summed into grad_e at the
+  // end; the SIMT path one [N][D] (none when grad_e itself is fp32).
+  if (!(flags & CCE_NEED_DE)) p.acc_bytes = 0;
+  else if (tc) p.acc_bytes = align_up(2 * (size_t)N * (size_t)D * 4);
+  else p.acc_bytes = (flags & CCE_DE_F32) ? 0 : align_up((size_t)N * (size_t)D * 4);
   // three tile counters per vocabulary chunk for the dynamically scheduled kernels
   p.counter_bytes = align_up((size_t)cce::ceil_div(V > 0 ? V : 1, vc) * 3 * sizeof(int));
   p.scale_bytes = (tc && dtype == CCE_F16) ? kAlign : 0;  // {s, 1/s} for fp16 dlogits
@@ -115,7 +125,7 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
 }
 
 size_t plan_bytes(const BwdPlan& p) {
-  return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes;
+  return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes + p.keep_t_bytes;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -200,10 +210,13 @@ int cce_device_status(int reset) {
 
 int64_t cce_num_stat_tiles(int64_t V) { return V <= 0 ? 0 : cce::ceil_div(V, cce::kStatTile); }
 
+// The LSE partials (max, sum-exp) per row per kernel tile: 2 x ceil(V / 128) x N
+// floats covers both kernel families (tensor-core tiles are 256 columns wide).
 size_t cce_forward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
   (void)D;
   (void)dtype;
-  return align_up((size_t)cce_num_stat_tiles(V) * (size_t)(N > 0 ? N : 0) * sizeof(float));
+  const int64_t P = V > 0 ? cce::ceil_div(V, cce::kSimtLseTile) : 0;
+  return align_up(2 * (size_t)P * (size_t)(N > 0 ? N : 0) * sizeof(float));
 }
 
 int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
@@ -223,17 +236,19 @@ int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
   rc = check_arch();
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  cce::FwdArgs a{e, c, bias, bias_dtype, targets, N, D, V, v_offset, dtype, tile_max,
-                 (float*)workspace, tgt};
+  const bool tc = !force_simt() && cce::tc_supported(e, c, D, dtype);
+  const int64_t P = cce::ceil_div(V, tc ? cce::kTcLseTile : cce::kSimtLseTile);
+  float* part_m = (float*)workspace;
+  float* part_s = part_m + P * N;
+  cce::FwdArgs a{e, c, bias, bias_dtype, targets, N, D, V, v_offset, dtype, tile_max, part_m, part_s, tgt};
   // Rows whose target is not in this call's vocabulary range keep tgt = 0.
   CCE_CUDA_CHECK(cudaMemsetAsync(tgt, 0, (size_t)N * sizeof(float), s), "cce_forward memset");
-  if (!force_simt() && cce::tc_supported(e, c, D, dtype)) {
+  if (tc) {
     CCE_CUDA_CHECK(cce::tc_forward(a, s), "cce_forward tc kernel");
   } else {
     CCE_CUDA_CHECK(cce::simt_forward(a, s), "cce_forward simt kernel");
   }
-  CCE_CUDA_CHECK(cce::launch_lse_combine(tile_max, (const float*)workspace, nullptr,
-                                         cce_num_stat_tiles(V), N, N, lse, nullptr, nullptr, s),
+  CCE_CUDA_CHECK(cce::launch_lse_combine(part_m, part_s, nullptr, P, N, N, lse, nullptr, nullptr, s),
                  "cce_forward combine");
   return CCE_OK;
 }
@@ -305,19 +320,24 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   uint8_t* keep = (uint8_t*)ws;
   void* dl = ws + p.keep_bytes;
   float* acc = nullptr;
-  if (need_de) acc = (flags & CCE_DE_F32) ? (float*)grad_e : (float*)(ws + p.keep_bytes + p.dl_bytes);
+  if (need_de)
+    acc = (!p.tc && (flags & CCE_DE_F32)) ? (float*)grad_e : (float*)(ws + p.keep_bytes + p.dl_bytes);
   int* counters = (int*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes);
   float* scale = p.scale_bytes ? (float*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes)
                                : nullptr;
+  uint32_t* keep_t = p.keep_t_bytes
+                         ? (uint32_t*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes)
+                         : nullptr;
   if (p.tc) CCE_CUDA_CHECK(cudaMemsetAsync(counters, 0, p.counter_bytes, s), "cce_backward memset counters");
+  if (keep_t) CCE_CUDA_CHECK(cudaMemsetAsync(keep_t, 0, p.keep_t_bytes, s), "cce_backward memset mask table");
   if (scale) CCE_CUDA_CHECK(cce::launch_pow2_absmax(d_nll, N, scale, s), "cce_backward scale");
 
   CCE_CUDA_CHECK(cce::launch_block_mask(tile_max, lse, targets, d_nll, N, V, v_offset, filter_log_eps,
-                                        (flags & CCE_NO_FILTER) != 0, keep, skip_stats, s),
+                                        (flags & CCE_NO_FILTER) != 0, keep, keep_t, p.keep_t_ld, skip_stats, s),
                  "cce_backward mask");
   if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
 
-  cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, N, D, V, v_offset, dtype,
+  cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, keep_t, p.keep_t_ld, N, D, V, v_offset, dtype,
                       0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr, scale};
   const int64_t nchunks = cce::ceil_div(V, p.vc);
   SideStreams* ss = nullptr;
@@ -345,9 +365,11 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
       CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->ev_l, 0), "cce_backward wait");
       CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->ev_l, 0), "cce_backward wait");
       if (need_de) {
-        const bool write_out = last && !(flags & CCE_DE_F32);
-        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, write_out ? grad_e : nullptr, write_out, ss->se),
-                       "cce_backward tc grad_e");
+        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, ss->se), "cce_backward tc grad_e");
+        if (last)
+          CCE_CUDA_CHECK(cce::launch_sum2_f32(acc, acc + N * D, grad_e, (flags & CCE_DE_F32) ? CCE_F32 : dtype,
+                                              N * D, ss->se),
+                         "cce_backward sum grad_e");
       }
       if (need_dc) CCE_CUDA_CHECK(cce::tc_grad_c(a, grad_c, ss->sc), "cce_backward tc grad_c");
       CCE_CUDA_CHECK(cudaEventRecord(ss->ev_e, ss->se), "cce_backward record");

@@ -21,8 +21,9 @@ struct FwdArgs {
   const int32_t* targets;
   int64_t N, D, V, v_offset;
   int dtype;
-  float* tile_max;  // [nVt][N]
-  float* tile_sum;  // [nVt][N] (workspace)
+  float* tile_max;  // [ceil(V / kStatTile)][N]: row max over each statistics tile (filter input)
+  float* part_m;    // [P][N] (workspace): row max over each kernel tile, P = ceil(V / lse_tile)
+  float* part_s;    // [P][N] (workspace): row sum of exp(logit - part_m) over the same columns
   float* tgt;       // [N]
 };
 
@@ -35,6 +36,9 @@ struct BwdChunkArgs {
   const float* lse;
   const float* d_nll;
   const uint8_t* keep;   // [nRb][nVt] block mask
+  const uint32_t* keep_t;  // [ceil(V/128)][keep_t_ld] words: bit r of row m = a kept block of
+                           // row block r in the 128 vocabulary columns of m (grad_c's M tiles)
+  int64_t keep_t_ld;
   int64_t N, D, V, v_offset;
   int dtype;
   int64_t vc0;           // first local vocab row of the chunk
@@ -54,15 +58,20 @@ cudaError_t launch_lse_combine(const float* part_max, const float* part_sum, con
                                cudaStream_t stream);
 cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int32_t* targets,
                               const float* d_nll, int64_t N, int64_t V, int64_t v_offset,
-                              float log_eps, bool no_filter, uint8_t* keep, int64_t* skip_stats,
-                              cudaStream_t stream);
+                              float log_eps, bool no_filter, uint8_t* keep, uint32_t* keep_t,
+                              int64_t keep_t_ld, int64_t* skip_stats, cudaStream_t stream);
 cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, cudaStream_t stream);
+// dst[i] = a[i] + b[i], written in dtype (CCE_F32 / F16 / BF16)
+cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype, int64_t n, cudaStream_t stream);
 // out[0] = s = the power of two >= max |x| (1 if all zero), out[1] = 1 / s
 cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t stream);
 
 // ---- SIMT kernels (simt_kernels.cu): any dtype, any shape ----
 cudaError_t simt_forward(const FwdArgs& a, cudaStream_t stream);
+// vocabulary columns per LSE partial of simt_forward / tc_forward
+constexpr int64_t kSimtLseTile = 128;
+constexpr int64_t kTcLseTile = 256;
 cudaError_t simt_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
 // grad_e_acc[N, D] (+)= dl[N, vc_len] @ c[v_offset-local rows vc0.., D]
 cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, cudaStream_t stream);
@@ -77,8 +86,10 @@ bool tc_backward_supported(const void* e, const void* c, int64_t D, int dtype);
 int tc_read_status(bool reset);
 cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
 cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
-cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
-                      bool write_out, cudaStream_t stream);
+// acc2[2][N][D] fp32: each output tile's two K halves of this chunk are
+// stored (accumulate = false) or added into slabs 0 and 1; grad_e is
+// acc2[0] + acc2[1] after the last chunk (launch_sum2_f32).
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t stream);
 cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
 
 }  // namespace cce

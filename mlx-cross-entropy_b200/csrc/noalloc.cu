@@ -22,8 +22,9 @@
 
 namespace {
 
-// Capacity in floats: ceil(V / 64) * N must not exceed it (e.g. V = 128256
-// with N up to 4185, or V = 256000 with N up to 2097).
+// Capacity in floats: the forward's LSE partials, 2 * ceil(V / 128) * N, must
+// not exceed it (e.g. V = 128256 with N up to 4185, or V = 256000 with N up
+// to 2097).
 constexpr int64_t kMaxScratchFloats = 8ll << 20;
 
 static __device__ __align__(256) float g_fwd_scratch[kMaxScratchFloats];
@@ -59,11 +60,11 @@ int cce_forward_noalloc(const void* e, const void* c, const void* bias, int bias
                         const int32_t* targets, int64_t N, int64_t D, int64_t V, int64_t v_offset,
                         int dtype, float* tile_max, float* lse, float* tgt, void* stream) {
   if (N < 0 || V < 0) return cce::report_error(CCE_ERR_SHAPE, "cce_forward_noalloc: negative size");
-  const int64_t need = cce_num_stat_tiles(V) * N;
+  const int64_t need = (int64_t)(cce_forward_workspace_bytes(N, D, V, dtype) / sizeof(float));
   if (need > kMaxScratchFloats) {
     char msg[256];
     snprintf(msg, sizeof(msg),
-             "cce_forward_noalloc: ceil(V/64) * N = %lld partials exceed the static scratch of "
+             "cce_forward_noalloc: 2 * ceil(V/128) * N = %lld partials exceed the static scratch of "
              "%lld floats (32 MiB); use cce_forward with a caller-allocated workspace",
              (long long)need, (long long)kMaxScratchFloats);
     return cce::report_error(CCE_ERR_WORKSPACE, msg);

@@ -14,7 +14,12 @@ namespace cce {
 namespace {
 
 constexpr int BM = 64;     // rows of a forward / dlogits tile
-constexpr int BN = 128;    // vocabulary columns of a tile (= one tile statistic)
+constexpr int BN = 128;    // vocabulary columns of a tile
+constexpr int SG = BN / kStatTile;  // statistics tiles per tile
+static_assert(BN == kSimtLseTile, "one LSE partial per tile");
+static_assert(kStatTile % 16 == 0 && BN % kStatTile == 0, "tile / statistics-tile layout");
+// statistics tile (within the tile) of thread column tx + 16 j, tx < 16
+__device__ __forceinline__ constexpr int gof(int j) { return (16 * j) / kStatTile; }
 constexpr int BK = 16;
 constexpr int THREADS = 256;
 
@@ -81,7 +86,8 @@ template <typename T, typename TB>
 __global__ void __launch_bounds__(THREADS)
 simt_fwd_kernel(const T* __restrict__ e, const T* __restrict__ c, const void* __restrict__ bias,
                 const int32_t* __restrict__ targets, int64_t N, int64_t D, int64_t V, int64_t v_offset,
-                float* __restrict__ tile_max, float* __restrict__ tile_sum, float* __restrict__ tgt) {
+                float* __restrict__ tile_max, float* __restrict__ part_m, float* __restrict__ part_s,
+                float* __restrict__ tgt) {
   const int64_t r0 = (int64_t)blockIdx.x * BM;
   const int64_t tile = blockIdx.y;
   const int64_t v0 = tile * BN;
@@ -94,40 +100,49 @@ simt_fwd_kernel(const T* __restrict__ e, const T* __restrict__ c, const void* __
     const int64_t v = v0 + tx + 16 * j;
     bv[j] = (bias != nullptr && v < V) ? bias_at<TB>(bias, v) : 0.f;
   }
-  // columns tx + 16 j: j < 4 lie in the tile's first 64-column statistics
-  // tile, j >= 4 in the second
+  // column tx + 16 j (tx < 16) lies in the tile's statistics tile 16 j / kStatTile
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t row = r0 + ty + 16 * i;
     float x[8];
-    float m[2] = {-INFINITY, -INFINITY};
+    float m[SG];
+#pragma unroll
+    for (int g = 0; g < SG; ++g) m[g] = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int64_t v = v0 + tx + 16 * j;
       x[j] = (v < V) ? acc[i][j] + bv[j] : -INFINITY;
-      m[j >> 2] = fmaxf(m[j >> 2], x[j]);
+      m[gof(j)] = fmaxf(m[gof(j)], x[j]);
     }
 #pragma unroll
-    for (int g = 0; g < 2; ++g)
+    for (int g = 0; g < SG; ++g)
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
-    float s[2] = {0.f, 0.f};
+    float s[SG];
+#pragma unroll
+    for (int g = 0; g < SG; ++g) s[g] = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (m[j >> 2] != -INFINITY) s[j >> 2] += exp2f((x[j] - m[j >> 2]) * kLog2e);
+      if (m[gof(j)] != -INFINITY) s[gof(j)] += exp2f((x[j] - m[gof(j)]) * kLog2e);
 #pragma unroll
-    for (int g = 0; g < 2; ++g)
+    for (int g = 0; g < SG; ++g)
 #pragma unroll
       for (int o = 8; o >= 1; o >>= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
     if (row < N) {
       if (tx == 0) {
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
-          if (v0 + g * kStatTile < V) {
-            tile_max[(2 * tile + g) * N + row] = m[g];
-            tile_sum[(2 * tile + g) * N + row] = s[g];
-          }
-        }
+        for (int g = 0; g < SG; ++g)
+          if (v0 + g * kStatTile < V) tile_max[(SG * tile + g) * N + row] = m[g];
+        // the tile's LSE partial: fold the statistics tiles' (max, sum-exp)
+        float M = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < SG; ++g) M = fmaxf(M, m[g]);
+        float S = 0.f;
+#pragma unroll
+        for (int g = 0; g < SG; ++g)
+          if (m[g] != -INFINITY) S += s[g] * exp2f((m[g] - M) * kLog2e);
+        part_m[tile * N + row] = M;
+        part_s[tile * N + row] = S;
       }
       const int64_t tl = (int64_t)targets[row] - v_offset;
 #pragma unroll
@@ -149,11 +164,13 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
   const int64_t vend = min(vc0 + vc_len, V);
   const int64_t nVt = ceil_div(V, kStatTile);
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  // the tile's two 64-column statistics tiles
+  // the tile's SG statistics tiles
   const uint8_t* kr = keep + (r0 / kRowBlock) * nVt + v0 / kStatTile;
-  const bool kept0 = kr[0] != 0;
-  const bool kept1 = (v0 / kStatTile + 1 < nVt) && kr[1] != 0;
-  if (!kept0 && !kept1) {
+  uint32_t kmask = 0;
+#pragma unroll
+  for (int g = 0; g < SG; ++g)
+    if (v0 / kStatTile + g < nVt && kr[g] != 0) kmask |= 1u << g;
+  if (kmask == 0) {
     for (int idx = threadIdx.x; idx < BM * BN; idx += THREADS) {
       const int r = idx / BN, cc = idx % BN;
       const int64_t row = r0 + r, v = v0 + cc;
@@ -189,7 +206,7 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
       const int64_t v = v0 + tx + 16 * j;
       if (v < vend) {
         float w = 0.f;
-        if (j < 4 ? kept0 : kept1) {
+        if ((kmask >> gof(j)) & 1u) {
           w = g * exp2f((acc[i][j] + bv[j] - L) * kLog2e);
           if (v == tl) w -= g;
         }
@@ -282,15 +299,15 @@ cudaError_t fwd_dispatch_bias(const FwdArgs& a, cudaStream_t s) {
   switch (a.bias == nullptr ? CCE_F32 : a.bias_dtype) {
     case CCE_F32:
       simt_fwd_kernel<T, float><<<grid, THREADS, 0, s>>>(e, c, a.bias, a.targets, a.N, a.D, a.V,
-                                                          a.v_offset, a.tile_max, a.tile_sum, a.tgt);
+                                                          a.v_offset, a.tile_max, a.part_m, a.part_s, a.tgt);
       break;
     case CCE_F16:
       simt_fwd_kernel<T, __half><<<grid, THREADS, 0, s>>>(e, c, a.bias, a.targets, a.N, a.D, a.V,
-                                                           a.v_offset, a.tile_max, a.tile_sum, a.tgt);
+                                                           a.v_offset, a.tile_max, a.part_m, a.part_s, a.tgt);
       break;
     case CCE_BF16:
       simt_fwd_kernel<T, __nv_bfloat16><<<grid, THREADS, 0, s>>>(
-          e, c, a.bias, a.targets, a.N, a.D, a.V, a.v_offset, a.tile_max, a.tile_sum, a.tgt);
+          e, c, a.bias, a.targets, a.N, a.D, a.V, a.v_offset, a.tile_max, a.part_m, a.part_s, a.tgt);
       break;
     default:
       return cudaErrorInvalidValue;

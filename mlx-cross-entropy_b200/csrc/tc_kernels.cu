@@ -46,6 +46,15 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
+// Statistics tiles (kStatTile vocabulary columns each, the filter's column
+// granularity) per engine tile and per K-block.
+constexpr int kGroups = BN / kStatTile;                // per 256-column output tile
+constexpr uint32_t kAllGroups = (1u << kGroups) - 1u;
+constexpr int kChunksPerStat = kStatTile / 32;         // epilogue 32-column chunks per statistics tile
+constexpr int kStatsPerM = BM / kStatTile;             // per 128-row M tile (grad_c)
+constexpr int kStepsPerStat = kStatTile / 16;          // K=16 MMA steps per statistics tile (grad_e)
+static_assert(kStatTile % 32 == 0 && BK % kStatTile == 0 && kGroups <= 32, "statistics-tile layout");
+static_assert(BN == kTcLseTile, "one LSE partial per output tile");
 constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-mask slice (bits)
 constexpr uint32_t OUT_STAGE_BYTES = 4 * 4096;  // epilogue output staging, 4 KB per epilogue warp
 constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
@@ -56,11 +65,18 @@ struct Sched {
   int a3d, b3d;  // MN-major operand loaded as one 3-D box (else one 2-D box per 64 columns)
   int* counter;  // dynamic scheduling: next tile id (zeroed before the launch); nullptr = static
   int group;     // grouped raster: blocks of the fast dimension per group (<= 0: all)
-  // Tile id -> (mb, nb).  Ids walk the fast dimension inside groups of `group`
+  int ksplit;    // K splits per output tile (<= 1: none); split s is its own work unit
+  __host__ __device__ __forceinline__ int splits() const { return ksplit > 1 ? ksplit : 1; }
+  __host__ __device__ __forceinline__ int units() const { return num_m * num_n * splits(); }
+  // Unit id -> (mb, nb, ks).  All units of split 0 come first, then split 1, ...
+  // Within a split, ids walk the fast dimension inside groups of `group`
   // blocks, then the slow dimension, then the next group: the ~148 tiles in
   // flight cover group x (148 / group) blocks, so both operand panels of the
   // window stay in L2 even when one operand as a whole does not.
-  __device__ __forceinline__ void coords(int tile, int& mb, int& nb) const {
+  __device__ __forceinline__ void coords(int unit, int& mb, int& nb, int& ks) const {
+    const int per_split = num_m * num_n;
+    ks = unit / per_split;
+    const int tile = unit - ks * per_split;
     const int fast = m_fast ? num_m : num_n;
     const int slow = m_fast ? num_n : num_m;
     const int gsz0 = (group > 0 && group < fast) ? group : fast;
@@ -78,6 +94,12 @@ struct Sched {
       mb = sl;
     }
   }
+  // K-blocks [kb0, kb1) of split ks.
+  __device__ __forceinline__ void krange(int ks, int& kb0, int& kb1) const {
+    const int per = (num_kb + splits() - 1) / splits();
+    kb0 = min(ks * per, num_kb);
+    kb1 = min(kb0 + per, num_kb);
+  }
 };
 
 // Fast-dimension group size: all blocks when that operand fits comfortably in
@@ -90,13 +112,40 @@ int raster_group(int64_t fast_operand_bytes) {
 // tile]: bits in shared memory (row-aligned 32-bit words, `wpr` per row) when
 // they fit, else the bytes in global memory (row stride `ld`).
 struct MaskView {
-  const uint32_t* bits;
+  const uint32_t* bits;  // row-aligned words (zero past `cols`), shared or global memory
   const uint8_t* bytes;
   int64_t ld;
   int wpr;
+  int cols;
   __device__ __forceinline__ bool get(int r, int c) const {
     if (bits) return (bits[r * wpr + (c >> 5)] >> (c & 31)) & 1u;
     return bytes[(int64_t)r * ld + c] != 0;
+  }
+  // Bits [c, c + n) of row r (n <= 32 divides 32, c a multiple of n).
+  __device__ __forceinline__ uint32_t field(int r, int c, int n) const {
+    const uint32_t lo = n == 32 ? 0xffffffffu : (1u << n) - 1u;
+    if (bits) return (bits[r * wpr + (c >> 5)] >> (c & 31)) & lo;
+    uint32_t m = 0;
+    for (int i = 0; i < n && c + i < cols; ++i) m |= (bytes[(int64_t)r * ld + c + i] != 0 ? 1u : 0u) << i;
+    return m;
+  }
+  // First set column of row r in [c, c1), else c1.
+  __device__ __forceinline__ int next(int r, int c, int c1) const {
+    if (bits) {
+      const uint32_t* row = bits + r * wpr;
+      while (c < c1) {
+        const uint32_t w = row[c >> 5] >> (c & 31);
+        if (w) {
+          c += __ffs(w) - 1;
+          return c < c1 ? c : c1;
+        }
+        c = (c | 31) + 1;
+      }
+      return c1;
+    }
+    for (; c < c1; ++c)
+      if (bytes[(int64_t)r * ld + c]) return c;
+    return c1;
   }
 };
 
@@ -180,9 +229,9 @@ struct Stager {
     slot ^= 1;
   }
 
-  // 32 fp32 values of this lane's row -> two 16 x 32 boxes at (x, y) and
-  // (x + 16, y), stored or added to global memory.
-  __device__ __forceinline__ void store_f32(const float (&v)[32], int x, int y, bool add) {
+  // 32 fp32 values of this lane's row -> two 16 x 32 x 1 boxes at (x, y, z)
+  // and (x + 16, y, z) of a 3-D map, stored or added to global memory.
+  __device__ __forceinline__ void store_f32(const float (&v)[32], int x, int y, int z, bool add) {
     acquire<0>();
 #pragma unroll
     for (int h = 0; h < 2; ++h)
@@ -194,8 +243,8 @@ struct Stager {
     if ((threadIdx.x & 31) == 0) {
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (add) tma_reduce_add_2d(tm, smem_u32(buf + h * 2048), x + 16 * h, y);
-        else tma_store_2d(tm, smem_u32(buf + h * 2048), x + 16 * h, y);
+        if (add) tma_reduce_add_3d(tm, smem_u32(buf + h * 2048), x + 16 * h, y, z);
+        else tma_store_3d(tm, smem_u32(buf + h * 2048), x + 16 * h, y, z);
       }
       bulk_commit();
     }
@@ -210,30 +259,35 @@ template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
   const int32_t* targets;
   const void* bias;
-  float* tile_max;
-  float* tile_sum;
+  float* tile_max;  // [ceil(V / kStatTile)][N]
+  float* part_m;    // [ceil(V / BN)][N]
+  float* part_s;
   float* tgt;
   int64_t N, V, v_offset;
 
   struct State {
     int64_t row, tl, col0;
-    float m, s;
+    float m, s;  // online max / sum-exp over the whole tile (the LSE partial)
+    float mt;    // max over the current statistics tile
   };
 
   static constexpr bool kMask = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
-  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
-  __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
+  static constexpr bool kMaskBits = false;
+  __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
+  __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   template <class S>
   __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
 
-  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r, int) const {
     st.row = (int64_t)mb * BM + r;
     st.tl = st.row < N ? (int64_t)targets[st.row] - v_offset : -1;
     st.col0 = (int64_t)nb * BN;
     st.m = -INFINITY;
     st.s = 0.f;
+    st.mt = -INFINITY;
   }
 
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
@@ -261,19 +315,21 @@ struct FwdEpi {
       st.s = st.s * exp2f(fmaf(st.m, kLog2e, -nml)) + acc;
       st.m = nm;
     }
-    if ((c & 1) == 1) {  // end of a 64-column statistics tile
-      const int h = c >> 1;
-      if (st.row < N && st.col0 + h * kStatTile < V) {
-        const int64_t idx = (st.col0 / kStatTile + h) * N + st.row;
-        tile_max[idx] = st.m;
-        tile_sum[idx] = st.s;
-      }
-      st.m = -INFINITY;
-      st.s = 0.f;
+    st.mt = fmaxf(st.mt, mc);
+    if ((c + 1) % kChunksPerStat == 0) {  // end of a statistics tile
+      const int h = c / kChunksPerStat;
+      if (st.row < N && st.col0 + h * kStatTile < V) tile_max[(st.col0 / kStatTile + h) * N + st.row] = st.mt;
+      st.mt = -INFINITY;
     }
   }
 
-  __device__ __forceinline__ void end(State&) const {}
+  __device__ __forceinline__ void end(State& st) const {
+    if (st.row < N && st.col0 < V) {
+      const int64_t idx = (st.col0 / BN) * N + st.row;
+      part_m[idx] = st.m;
+      part_s[idx] = st.s;
+    }
+  }
 };
 
 // ---------------------------------------------------------------------------
@@ -289,9 +345,9 @@ struct DlogitsEpi {
   T* dl;                // [N][ld], column 0 = local vocab row vc0
   float* grad_bias;     // [V] or nullptr
   const float* scale;   // fp16: {s, 1/s}, dl holds w / s; nullptr = unscaled (bf16)
-  const uint8_t* mask_src;  // keep + vc0 / 64: the chunk's columns of the [nRb][nVt] mask
+  const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
   int64_t mask_ld;          // nVt
-  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
+  int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
   int64_t N, V, v_offset, vc0, vc_end, ld;
   // 1: every 64-column group of an active tile is written (the CTA-pair grad
   // GEMMs read whole 256-row tiles); 0: only 128-column halves holding a kept
@@ -309,15 +365,7 @@ struct DlogitsEpi {
   static constexpr bool kMask = true;
   // Kept 64-column groups of the tile (bit g = chunk stat tile 4 nb + g).
   __device__ __forceinline__ uint32_t group_mask(const MaskView& mk, int mb, int nb) const {
-    uint32_t m = 0;
-    if (mb < mask_rows) {
-#pragma unroll
-      for (int g = 0; g < BN / kStatTile; ++g) {
-        const int t = (BN / kStatTile) * nb + g;
-        if (t < mask_cols && mk.get(mb, t)) m |= 1u << g;
-      }
-    }
-    return m;
+    return mb < mask_rows ? mk.field(mb, kGroups * nb, kGroups) : 0u;
   }
   __device__ __forceinline__ bool tile_active(const MaskView& mk, int mb, int nb) const {
     return group_mask(mk, mb, nb) != 0;
@@ -325,15 +373,19 @@ struct DlogitsEpi {
   // 64-column groups the MMA computes: only the kept ones (the epilogue never
   // reads the accumulator columns of the others).
   __device__ __forceinline__ uint32_t col_mask(const MaskView& mk, int mb, int nb) const {
-    return all_groups ? 0xFu : group_mask(mk, mb, nb);
+    return all_groups ? kAllGroups : group_mask(mk, mb, nb);
   }
-  __device__ __forceinline__ bool chunk_live(const State& st, int c) const { return (st.kmask >> (c >> 1)) & 1u; }
-  __device__ __forceinline__ bool kb_active(const MaskView&, int, int, int) const { return true; }
+  __device__ __forceinline__ bool chunk_live(const State& st, int c) const {
+    return (st.kmask >> (c / kChunksPerStat)) & 1u;
+  }
+  static constexpr bool kMaskBits = false;
+  __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
+  __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
 
   // Rejected tiles are not written: the grad GEMMs skip exactly those blocks.
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
 
-  __device__ __forceinline__ void begin(State& st, const MaskView& mk, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView& mk, int mb, int nb, int r, int) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = vc0 + (int64_t)nb * BN;  // local vocab id of the tile's column 0
     const bool ok = st.row < N;
@@ -347,7 +399,7 @@ struct DlogitsEpi {
 
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
     const int64_t cb = st.col0 + c * 32;
-    const bool kept = (st.kmask >> (c >> 1)) & 1u;
+    const bool kept = (st.kmask >> (c / kChunksPerStat)) & 1u;
     float b[32];
     if constexpr (!std::is_void<TB>::value) {
       load_bias32<TB>(bias, cb, vc_end, b);
@@ -365,7 +417,11 @@ struct DlogitsEpi {
       }
       v[j] = w;
     }
-    if (all_groups || ((st.kmask >> (2 * (c >> 2))) & 3u)) sg.store16<T>(v, (int)(cb - vc0), st.y0);
+    // grad_c multiplies whole 128-column quarters (its M tiles): a quarter
+    // with a kept group is stored whole (zeros in the others), the rest never
+    // read; grad_e reads kept groups only.
+    if (all_groups || ((st.kmask >> (kStatsPerM * (c >> 2))) & ((1u << kStatsPerM) - 1u)))
+      sg.store16<T>(v, (int)(cb - vc0), st.y0);
     if (grad_bias != nullptr) {
       const int lane = threadIdx.x & 31;
       const float colsum = warp_transpose_sum32(v);
@@ -380,65 +436,61 @@ struct DlogitsEpi {
 // K5: grad_e accumulation
 // ---------------------------------------------------------------------------
 
-template <typename T>
+// Each output tile's K range (the chunk's vocabulary rows) is split in two
+// work units; split s adds into fp32 accumulator slab s of acc[2][N][D] (a TMA
+// store in the first chunk, a TMA reduce-add after it), so every slab has one
+// writer per chunk and the sums are deterministic.  The caller adds the two
+// slabs into grad_e after the last chunk.
 struct GradEEpi {
-  float* acc;   // [N, D] fp32 accumulator
-  T* out;       // [N, D] final output (write_out)
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
-  const uint8_t* mask_src;  // keep + vc0 / 64: the chunk's columns of the [nRb][nVt] mask
+  const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
   int64_t mask_ld;          // nVt
-  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
-  int64_t N, D;
-  int accumulate, write_out;
+  int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
+  int accumulate;
 
   struct State {
-    int64_t row, col0;
+    int64_t col0;
     float s;
     int y0;  // first row of this warp's 32-row slab
+    int ks;  // accumulator slab
   };
-  // K runs over the chunk's vocabulary rows: K-block kb (64 rows) is the
-  // chunk's stat tile kb.
+  // K runs over the chunk's vocabulary rows: K-block kb (64 rows) holds the
+  // chunk's statistics tiles BK / kStatTile * kb + i; the MMA skips the K=16
+  // steps of the rejected ones.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
-  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
-  __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
-    return mb < mask_rows && kb < mask_cols && mk.get(mb, kb);
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
+  static constexpr bool kMaskBits = false;
+  static constexpr int kSpk = BK / kStatTile;  // statistics tiles per K-block
+  // K=16 steps of K-block kb whose statistics tile the filter keeps (kb active).
+  __device__ __forceinline__ uint32_t ksub_mask(const MaskView& mk, int mb, int, int kb) const {
+    const uint32_t f = mk.field(mb, kSpk * kb, kSpk);
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < kSpk; ++i)
+      if ((f >> i) & 1u) m |= ((1u << kStepsPerStat) - 1u) << (i * kStepsPerStat);
+    return m;
+  }
+  // First K-block in [kb, kb1) with a kept statistics tile in row block mb, else kb1.
+  __device__ __forceinline__ int next_kb(const MaskView& mk, int mb, int, int kb, int kb1) const {
+    if (mb >= mask_rows) return kb1;
+    const int lim = min(kSpk * kb1, mask_cols);
+    const int t = mk.next(mb, kSpk * kb, lim);
+    return t < lim ? t / kSpk : kb1;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   template <class S>
   __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
-  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
-    st.row = (int64_t)mb * BM + r;
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r, int ks) const {
     st.col0 = (int64_t)nb * BN;
     st.s = scale ? scale[0] : 1.f;
-    st.y0 = (int)(st.row - (threadIdx.x & 31));
+    st.y0 = mb * BM + r - (int)(threadIdx.x & 31);
+    st.ks = ks;
   }
-  // Not the last chunk: the tile goes to the fp32 accumulator by TMA (a store
-  // for the first chunk, a reduce-add after it).  Last chunk: accumulator +
-  // tile -> T output.  The stager's tensor map is acc (fp32) or out (T).
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
-    const int64_t cb = st.col0 + c * 32;
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= st.s;
-    if (!write_out) {
-      sg.store_f32(v, (int)cb, st.y0, accumulate != 0);
-      return;
-    }
-    if (accumulate && st.row < N) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int64_t col = cb + g * 8;
-        if (col < D) {
-          const float* a = acc + st.row * D + col;
-          const float4 x0 = *reinterpret_cast<const float4*>(a);
-          const float4 x1 = *reinterpret_cast<const float4*>(a + 4);
-          float* o = v + g * 8;
-          o[0] += x0.x; o[1] += x0.y; o[2] += x0.z; o[3] += x0.w;
-          o[4] += x1.x; o[5] += x1.y; o[6] += x1.z; o[7] += x1.w;
-        }
-      }
-    }
-    sg.store16<T>(v, (int)cb, st.y0);
+    sg.store_f32(v, (int)(st.col0 + c * 32), st.y0, st.ks, accumulate != 0);
   }
   __device__ __forceinline__ void end(State&) const {}
 };
@@ -451,9 +503,9 @@ template <typename T>
 struct GradCEpi {
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
-  const uint8_t* mask_src;  // keep + vc0 / 64
-  int64_t mask_ld;          // nVt
-  int mask_rows, mask_cols; // nRb, stat tiles in the chunk
+  const void* mask_src;     // activity table rows of the chunk's M tiles: [ceil(V/128)][mask_ld] words
+  int64_t mask_ld;          // words per table row
+  int mask_rows, mask_cols; // M tiles in the chunk, nRb
   int64_t rows, D;
 
   struct State {
@@ -461,19 +513,27 @@ struct GradCEpi {
     float s;
     int y0;  // first row of this warp's 32-row slab
   };
-  // M tile mb covers the chunk's stat tiles 2 mb and 2 mb + 1; K-block kb (64
-  // rows) lies in row block kb / 2.
+  // M tile mb covers the chunk's statistics tiles kStatsPerM * mb + i; K-block
+  // kb (64 rows) lies in row block kb / 2.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
-  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return 0xFu; }
-  __device__ __forceinline__ bool kb_active(const MaskView& mk, int mb, int, int kb) const {
-    const int t = 2 * mb;
-    return (t < mask_cols && mk.get(kb >> 1, t)) || (t + 1 < mask_cols && mk.get(kb >> 1, t + 1));
+  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
+  // The mask view is the transposed activity table: row = the chunk's 128-row
+  // M tile, bit = row block (the OR of the tile's statistics tiles there).
+  static constexpr bool kMaskBits = true;
+  static constexpr int kKpr = kRowBlock / BK;  // K-blocks per row block
+  __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
+  __device__ __forceinline__ int next_kb(const MaskView& mk, int mb, int, int kb, int kb1) const {
+    if (mb >= mask_rows) return kb1;
+    const int lim = min((kb1 + kKpr - 1) / kKpr, mask_cols);
+    const int r = mk.next(mb, kb / kKpr, lim);
+    if (r >= lim) return kb1;
+    return max(kb, r * kKpr);
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   template <class S>
   __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
-  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r) const {
+  __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r, int) const {
     st.row = (int64_t)mb * BM + r;
     st.col0 = (int64_t)nb * BN;
     st.s = scale ? scale[0] : 1.f;
@@ -490,6 +550,52 @@ struct GradCEpi {
 // ---------------------------------------------------------------------------
 // the engine
 // ---------------------------------------------------------------------------
+
+// The epilogue's mask slice as a MaskView: copied into shared memory as bits
+// when it fits (all threads of the block take part; a __syncthreads follows
+// before any use), else read in place.  kMaskBits: the source already holds
+// row-aligned bit words (row stride mask_ld words); else one byte per entry
+// (row stride mask_ld bytes).
+template <class Epi>
+__device__ __forceinline__ void load_mask_view(const Epi& epi, uint8_t* smask, MaskView& mk) {
+  if constexpr (Epi::kMask) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows = epi.mask_rows, cols = epi.mask_cols;
+    const int wpr = (cols + 31) / 32;
+    const bool fits = (int64_t)rows * wpr * 4 <= SMASK_BYTES;
+    uint32_t* sb = reinterpret_cast<uint32_t*>(smask);
+    mk.cols = cols;
+    if constexpr (Epi::kMaskBits) {
+      const uint32_t* src = static_cast<const uint32_t*>(epi.mask_src);
+      if (fits) {
+        for (int i = threadIdx.x; i < rows * wpr; i += blockDim.x)
+          sb[i] = __ldg(src + (int64_t)(i / wpr) * epi.mask_ld + i % wpr);
+        mk.bits = sb;
+        mk.wpr = wpr;
+      } else {
+        mk.bits = src;
+        mk.wpr = (int)epi.mask_ld;
+      }
+    } else {
+      const uint8_t* src0 = static_cast<const uint8_t*>(epi.mask_src);
+      if (fits) {
+        for (int rr = warp; rr < rows; rr += blockDim.x / 32) {
+          const uint8_t* src = src0 + (int64_t)rr * epi.mask_ld;
+          for (int c0 = 0; c0 < cols; c0 += 32) {
+            const int cc = c0 + lane;
+            const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
+            if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
+          }
+        }
+        mk.bits = sb;
+        mk.wpr = wpr;
+      } else {
+        mk.bytes = src0;
+        mk.ld = epi.mask_ld;
+      }
+    }
+  }
+}
 
 template <bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -514,7 +620,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = sched.num_m * sched.num_n;
+  const int num_tiles = sched.units();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -534,27 +640,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     prefetch_tmap(&tmB);
   }
   // Filter-mask slice: copied to shared memory when it fits, else read in place.
-  MaskView mk{nullptr, nullptr, 0, 0};
-  if constexpr (Epi::kMask) {
-    const int rows = epi.mask_rows, cols = epi.mask_cols;
-    const int wpr = (cols + 31) / 32;
-    if ((int64_t)rows * wpr * 4 <= SMASK_BYTES) {
-      uint32_t* sb = reinterpret_cast<uint32_t*>(smask);
-      for (int rr = warp; rr < rows; rr += kThreads / 32) {
-        const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
-        for (int c0 = 0; c0 < cols; c0 += 32) {
-          const int cc = c0 + lane;
-          const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
-          if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
-        }
-      }
-      mk.bits = sb;
-      mk.wpr = wpr;
-    } else {
-      mk.bytes = epi.mask_src;
-      mk.ld = epi.mask_ld;
-    }
-  }
+  MaskView mk{nullptr, nullptr, 0, 0, 0};
+  load_mask_view<Epi>(epi, smask, mk);
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
@@ -580,12 +667,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         mbar_arrive(rfull + slot);
         if (tile < 0) break;
         next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (i + 1) * (int)gridDim.x;
-        int mb, nb;
-        sched.coords(tile, mb, nb);
+        int mb, nb, ks, kb0, kb1;
+        sched.coords(tile, mb, nb, ks);
+        sched.krange(ks, kb0, kb1);
         if (!epi.tile_active(mk, mb, nb)) continue;
         bool ok = true;
-        for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!epi.kb_active(mk, mb, nb, kb)) continue;
+        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
           uint8_t* a = sA + stage * A_BYTES;
@@ -641,20 +728,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int tile = ring[slot];
         mbar_arrive(rempty + slot);
         if (tile < 0) break;
-        int mb, nb;
-        sched.coords(tile, mb, nb);
+        int mb, nb, ks, kb0, kb1;
+        sched.coords(tile, mb, nb, ks);
+        sched.krange(ks, kb0, kb1);
         if (!epi.tile_active(mk, mb, nb)) continue;
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        // The tile's 64-column groups to compute: when they form one run of
-        // consecutive groups (j0, n0), one MMA of N = 64 n0 columns at B rows
-        // 64 j0 (K-major B: 8 KB per 64 rows); else the whole tile.  (Two
-        // runs as two MMAs re-read A from shared memory and measured slower.)
-        uint32_t j0 = 0, n0 = BN / 64;
+        // The tile's statistics-tile column groups to compute: when they form
+        // one run of consecutive groups (j0, n0), one MMA of N = kStatTile n0
+        // columns at B rows kStatTile j0 (K-major B: 128 bytes per row); else
+        // the whole tile.  (Two runs as two MMAs re-read A from shared memory
+        // and measured slower.)
+        uint32_t j0 = 0, n0 = kGroups;
         if constexpr (!B_MN) {
           const uint32_t cm = epi.col_mask(mk, mb, nb);
-          if (cm != 0xFu) {
+          if (cm != kAllGroups) {
             const uint32_t j = __ffs(cm) - 1;
             const uint32_t n = __ffs(~(cm >> j)) - 1;
             if ((cm >> (j + n)) == 0u) {
@@ -663,21 +752,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
           }
         }
-        const uint32_t idesc0 = idesc_with_n(idesc, 64 * n0);
+        const uint32_t idesc0 = idesc_with_n(idesc, kStatTile * n0);
+        const uint32_t d0 = d_tmem + kStatTile * j0;
+        const uint32_t boff = (kStatTile * 128u * j0) >> 4;
         bool ok = true;
-        uint32_t issued = 0;
-        for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!epi.kb_active(mk, mb, nb, kb)) continue;
+        uint32_t fresh = 1;  // the tile's first MMA overwrites the accumulator
+        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+          const uint32_t km = epi.ksub_mask(mk, mb, nb, kb);  // K=16 steps to issue
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
-          const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4);
+          const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4) + boff;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint32_t accf = (issued | (uint32_t)k) != 0 ? 1u : 0u;
-            mma_f16(d_tmem + 64 * j0, ad + k * a_kstep, bd + ((8192u * j0) >> 4) + k * b_kstep, idesc0, accf);
+            if ((km >> k) & 1u) {
+              mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
+              fresh = 0;
+            }
           }
-          ++issued;
           mma_commit(empty + stage);
           if (++stage == STAGES) {
             stage = 0;
@@ -704,18 +796,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int tile = ring[slot];
       mbar_arrive(rempty + slot);
       if (tile < 0) break;
-      int mb, nb;
-      sched.coords(tile, mb, nb);
+      int mb, nb, ks, kb0, kb1;
+      sched.coords(tile, mb, nb, ks);
+      sched.krange(ks, kb0, kb1);
       if (!epi.tile_active(mk, mb, nb)) {
         epi.inactive_tile(mb, nb, r);
         continue;
       }
       if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
       tc_fence_after();
-      bool any_kb = !Epi::kMask;
-      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = epi.kb_active(mk, mb, nb, kb);
+      const bool any_kb = !Epi::kMask || epi.next_kb(mk, mb, nb, kb0, kb1) < kb1;
       typename Epi::State st;
-      epi.begin(st, mk, mb, nb, r);
+      epi.begin(st, mk, mb, nb, r, ks);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -795,7 +887,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const uint32_t peer = rank ^ 1u;
-  const int num_tiles = sched.num_m * sched.num_n;
+  const int num_tiles = sched.units();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES2; ++s) {
@@ -814,27 +906,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  MaskView mk{nullptr, nullptr, 0, 0};
-  if constexpr (Epi::kMask) {
-    const int rows = epi.mask_rows, cols = epi.mask_cols;
-    const int wpr = (cols + 31) / 32;
-    if ((int64_t)rows * wpr * 4 <= SMASK_BYTES) {
-      uint32_t* sb = reinterpret_cast<uint32_t*>(smask);
-      for (int rr = warp; rr < rows; rr += kThreads / 32) {
-        const uint8_t* src = epi.mask_src + (int64_t)rr * epi.mask_ld;
-        for (int c0 = 0; c0 < cols; c0 += 32) {
-          const int cc = c0 + lane;
-          const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
-          if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
-        }
-      }
-      mk.bits = sb;
-      mk.wpr = wpr;
-    } else {
-      mk.bytes = epi.mask_src;
-      mk.ld = epi.mask_ld;
-    }
-  }
+  MaskView mk{nullptr, nullptr, 0, 0, 0};
+  load_mask_view<Epi>(epi, smask, mk);
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
     tmem_relinquish_pair();
@@ -849,8 +922,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   auto tile_on = [&](int mb, int nb) {
     return epi.tile_active(mk, 2 * mb, nb) || epi.tile_active(mk, 2 * mb + 1, nb);
   };
-  auto kb_on = [&](int mb, int nb, int kb) {
-    return epi.kb_active(mk, 2 * mb, nb, kb) || epi.kb_active(mk, 2 * mb + 1, nb, kb);
+  auto next_on = [&](int mb, int nb, int kb, int kb1) {
+    return min(epi.next_kb(mk, 2 * mb, nb, kb, kb1), epi.next_kb(mk, 2 * mb + 1, nb, kb, kb1));
   };
   const uint32_t full_leader = mapa_shared(smem_u32(full), 0);   // + 8 * stage
   const uint32_t rempty_leader = mapa_shared(smem_u32(rempty), 0);
@@ -884,14 +957,14 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
           mbar_arrive_cluster(rempty_leader + 8 * slot);
         }
         if (tile < 0) break;
-        int mb, nb;
-        sched.coords(tile, mb, nb);
+        int mb, nb, ks, kb0, kb1;
+        sched.coords(tile, mb, nb, ks);
+        sched.krange(ks, kb0, kb1);
         if (!tile_on(mb, nb)) continue;
         bool ok = true;
         const int arow = mb * 256 + (int)rank * 128;   // this CTA's A rows (or MN columns)
         const int bcol = nb * 256 + (int)rank * 128;   // this CTA's B columns
-        for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!kb_on(mb, nb, kb)) continue;
+        for (int kb = next_on(mb, nb, kb0, kb1); kb < kb1; kb = next_on(mb, nb, kb + 1, kb1)) {
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(full + stage, 2 * STAGE2_BYTES);
           const uint32_t fb = full_leader + 8 * stage;
@@ -949,16 +1022,16 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const int tile = ring[slot];
         mbar_arrive(rempty + slot);
         if (tile < 0) break;
-        int mb, nb;
-        sched.coords(tile, mb, nb);
+        int mb, nb, ks, kb0, kb1;
+        sched.coords(tile, mb, nb, ks);
+        sched.krange(ks, kb0, kb1);
         if (!tile_on(mb, nb)) continue;
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         uint32_t issued = 0;
-        for (int kb = 0; kb < sched.num_kb; ++kb) {
-          if (!kb_on(mb, nb, kb)) continue;
+        for (int kb = next_on(mb, nb, kb0, kb1); kb < kb1; kb = next_on(mb, nb, kb + 1, kb1)) {
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = adesc0 + (uint64_t)((stage * A2_BYTES) >> 4);
@@ -1004,8 +1077,9 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         mbar_arrive_cluster(rempty_leader + 8 * slot);
       }
       if (tile < 0) break;
-      int mb, nb;
-      sched.coords(tile, mb, nb);
+      int mb, nb, ks, kb0, kb1;
+      sched.coords(tile, mb, nb, ks);
+      sched.krange(ks, kb0, kb1);
       const int vmb = 2 * mb + (int)rank;   // this CTA's 128-row block
       if (!tile_on(mb, nb)) {
         epi.inactive_tile(vmb, nb, r);
@@ -1013,10 +1087,9 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       }
       if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
       tc_fence_after();
-      bool any_kb = !Epi::kMask;
-      for (int kb = 0; kb < sched.num_kb && !any_kb; ++kb) any_kb = kb_on(mb, nb, kb);
+      const bool any_kb = !Epi::kMask || next_on(mb, nb, kb0, kb1) < kb1;
       typename Epi::State st;
-      epi.begin(st, mk, vmb, nb, r);
+      epi.begin(st, mk, vmb, nb, r, ks);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -1154,6 +1227,23 @@ bool make_tmap_out(CUtensorMap* tm, const void* base, int dtype, int64_t inner, 
   return r == CUDA_SUCCESS;
 }
 
+// The two fp32 grad_e accumulator slabs acc2[2][N][D] as a 3-D map, written in
+// (16 x 32 x 1) boxes (64-byte rows, 64-byte swizzle); the slab index is the z
+// coordinate, so rows past N of one slab are clipped rather than spilling
+// into the other.
+bool make_tmap_acc2(CUtensorMap* tm, const float* acc2, int64_t D, int64_t N) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)N, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(D * 4), (cuuint64_t)(N * D * 4)};
+  cuuint32_t box[3] = {16, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(acc2), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <bool A_MN, bool B_MN, class Epi>
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
                         const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
@@ -1167,7 +1257,7 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
   }
-  const int tiles = s.num_m * s.num_n;
+  const int tiles = s.units();
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
@@ -1188,7 +1278,7 @@ cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const C
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
   }
-  const int tiles = s.num_m * s.num_n;
+  const int tiles = s.units();
   if (tiles == 0) return cudaSuccess;
   const int pairs = num_sms() / 2;
   const int grid = 2 * (tiles < pairs ? tiles : pairs);
@@ -1249,7 +1339,7 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, pair ? BN / 2 : BN)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            nullptr, raster_group(a.N * a.D * 2)};
-  FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.tile_sum, a.tgt, a.N, a.V, a.v_offset};
+  FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.part_m, a.part_s, a.tgt, a.N, a.V, a.v_offset};
   const CUtensorMap tmC{};  // the forward epilogue writes no tiles
   if (pair) return launch_gemm2<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
@@ -1310,26 +1400,20 @@ cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
 namespace {
 
 template <typename T>
-cudaError_t grad_e_launch(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
-                          bool write_out, cudaStream_t s) {
+cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t s) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmC;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
   const bool pair = use_pair();
   if (!make_tmap(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
   int b3d = 0;
   if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, (pair ? BN / 2 : BN) / 64, &b3d))
     return cudaErrorInvalidValue;
+  if (!make_tmap_acc2(&tmC, acc2, a.D, a.N)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
-           a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2)};
-  GradEEpi<T> epi{grad_e_acc, static_cast<T*>(grad_e_out), a.scale,
-                  a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
-                  (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
-                  a.N, a.D, accumulate ? 1 : 0, write_out ? 1 : 0};
-  CUtensorMap tmC;
-  const bool okC = write_out ? make_tmap_out(&tmC, grad_e_out, a.dtype, a.D, a.N, a.D)
-                             : make_tmap_out(&tmC, grad_e_acc, CCE_F32, a.D, a.N, a.D);
-  if (!okC) return cudaErrorInvalidValue;
+           a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2), 2};
+  GradEEpi epi{a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile), (int)ceil_div(a.N, kRowBlock),
+               (int)ceil_div(a.vc_len, kStatTile), accumulate ? 1 : 0};
   if (pair) return launch_gemm2<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
@@ -1345,8 +1429,8 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   Sched sc{(int)ceil_div(a.vc_len, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
            a.counters ? a.counters + 2 : nullptr, raster_group(a.N * a.D * 2)};
   GradCEpi<T> epi{static_cast<T*>(grad_c) + a.vc0 * a.D, a.scale,
-                  a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
-                  (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
+                  a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
+                  (int)ceil_div(a.vc_len, (int64_t)128), (int)ceil_div(a.N, kRowBlock),
                   a.vc_len, a.D};
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
@@ -1357,11 +1441,10 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
 
 }  // namespace
 
-cudaError_t tc_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, void* grad_e_out,
-                      bool write_out, cudaStream_t s) {
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t s) {
   if (a.N == 0 || a.D == 0) return cudaSuccess;
-  if (a.dtype == CCE_BF16) return grad_e_launch<__nv_bfloat16>(a, grad_e_acc, accumulate, grad_e_out, write_out, s);
-  if (a.dtype == CCE_F16) return grad_e_launch<__half>(a, grad_e_acc, accumulate, grad_e_out, write_out, s);
+  if (a.dtype == CCE_BF16) return grad_e_launch<__nv_bfloat16>(a, acc2, accumulate, s);
+  if (a.dtype == CCE_F16) return grad_e_launch<__half>(a, acc2, accumulate, s);
   return cudaErrorNotSupported;
 }
 

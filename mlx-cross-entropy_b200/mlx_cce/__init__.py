@@ -56,7 +56,7 @@ def cce_loss(e, c, targets, bias=None, reduction="mean", ignore_index=-100, *,
 
     e [N, D], c [V, D], targets [N]; returns a float32 scalar, or [N] for
     ``reduction='none'``.  ``skip_stats`` (optional CUDA int64[2]) accumulates
-    (skipped, total) 128-row x 64-column backward blocks.
+    (skipped, total) 128-row x 32-column backward blocks.
     """
     loss, lse = _cce(e, c, targets, bias, reduction, ignore_index, filter_log_eps, None, 0,
                      skip_stats)

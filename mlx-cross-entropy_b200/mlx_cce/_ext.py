@@ -35,7 +35,7 @@ CCE_ERR_WORKSPACE = -6
 CCE_ERR_ARG = -7
 
 CCE_F32, CCE_F16, CCE_BF16 = 0, 1, 2
-CCE_STAT_TILE = 64
+CCE_STAT_TILE = 32
 
 CCE_NEED_DE = 1
 CCE_NEED_DC = 2

@@ -31,24 +31,28 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_tile_count():
     assert _ext.version() == 100
-    assert _ext.num_stat_tiles(128256) == 2004
-    assert _ext.num_stat_tiles(64) == 1
-    assert _ext.num_stat_tiles(65) == 2
+    assert _ext.num_stat_tiles(128256) == 4008
+    assert _ext.num_stat_tiles(32) == 1
+    assert _ext.num_stat_tiles(33) == 2
     assert _ext.num_stat_tiles(0) == 0
 
 
 def test_workspace_sizes():
     lib = _ext.lib
     f = lib.cce_forward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16)
-    assert f >= 2004 * 4096 * 4 and f % 256 == 0
+    assert f >= 2 * 1002 * 4096 * 4 and f % 256 == 0
     flags = _ext.CCE_NEED_DE | _ext.CCE_NEED_DC
     b = lib.cce_backward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16, flags)
-    # mask + a bounded dlogits chunk (never [N, V]) + the fp32 grad_e accumulator
+    # mask + a bounded dlogits chunk (never [N, V]) + two fp32 grad_e accumulator slabs
     assert b < 4096 * 128256 * 2
-    assert b >= 4096 * 4096 * 4
+    assert b >= 2 * 4096 * 4096 * 4
     b32 = lib.cce_backward_workspace_bytes(4096, 4096, 128256, _ext.CCE_BF16,
                                            flags | _ext.CCE_DE_F32)
-    assert b32 < b
+    assert b32 <= b
+    # the fp32 (CUDA-core) path accumulates in grad_e itself when it is fp32
+    f = lib.cce_backward_workspace_bytes(512, 512, 32000, _ext.CCE_F32, flags)
+    f32 = lib.cce_backward_workspace_bytes(512, 512, 32000, _ext.CCE_F32, flags | _ext.CCE_DE_F32)
+    assert f32 == f - 512 * 512 * 4
 
 
 def test_error_codes_without_gpu_work():

@@ -66,7 +66,7 @@ def test_noalloc_forward_matches_workspace_forward_twice():
 
 
 def test_noalloc_rejects_calls_beyond_its_capacity():
-    # ceil(V / 64) * N above 8388608 partials: refused before any GPU work
+    # 2 * ceil(V / 128) * N above 8388608 partials: refused before any GPU work
     rc = _ext.lib.cce_forward_noalloc(None, None, None, 0, None, 4186, 4096, 128256, 0,
                                       _ext.CCE_BF16, None, None, None, None)
     assert rc == _ext.CCE_ERR_WORKSPACE
