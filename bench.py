@@ -47,13 +47,13 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-# DRAM bytes of one forward launch, measured by ncu on config 3 scaled to
-# V=32768 (profiles/forward_and_grad_e_cfg3_V32768_ncu.txt): e is read once
-# (33.6 MB); c and the tile statistics grow with V.
+# DRAM bytes (read + write) of one forward launch, measured by ncu on config 3
+# at full size (profiles/forward_cfg3_dram_traffic.txt): e is read once
+# (33.6 MB); c and the per-row statistics grow with the local vocabulary.
 def forward_traffic_bytes(N, D, V_local):
     if (N, D) != (4096, 4096):
         return None
-    return 33.55e6 + (302.276864e6 - 33.55e6 + 11.368704e6) * V_local / 32768
+    return 33.55e6 + (1168.373248e6 - 33.55e6) * V_local / 128256
 
 
 def env_int(name, default):
@@ -362,7 +362,10 @@ def run_ours(args, rank, world, local_rank):
                          "frac": fwd_tflops / peak,
                          "peak_kind": f"{src} bf16 {'sustained' if long_run else 'burst'}",
                          "traffic": traffic,
-                         "algorithmic_bytes": 2.0 * (N * D + vl * D) + 8.0 * N * (-(-vl // 32))},
+                         # e and c once, a max per row per 32-column statistics tile,
+                         # a (max, sum-exp) pair per row per 256-column kernel tile
+                         "algorithmic_bytes": (2.0 * (N * D + vl * D) + 4.0 * N * (-(-vl // 32))
+                                               + 8.0 * N * (-(-vl // 256)))},
             "e2e": {"value": N * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # library kernels per K steps (counted in the eager region; a graph
