@@ -122,8 +122,20 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
     tl[u] = live[u] ? (int64_t)targets[row] - v_offset : -1;
     tm[u] = tile_max + (live[u] ? row : 0);
   }
+  // all of this warp's tile maxima are loaded before any is tested, so the
+  // loads overlap
+  constexpr int kTilesPerWarp = kMaskTiles / kMaskWarps;
+  float x[kTilesPerWarp][kRowsPerLane];
+#pragma unroll
+  for (int q = 0; q < kTilesPerWarp; ++q) {
+    const int64_t j = (int64_t)blockIdx.x * kMaskTiles + warp + q * kMaskWarps;
+#pragma unroll
+    for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = (live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
+  }
   int skipped = 0, total = 0;
-  for (int w = warp; w < kMaskTiles; w += kMaskWarps) {
+#pragma unroll
+  for (int q = 0; q < kTilesPerWarp; ++q) {
+    const int w = warp + q * kMaskWarps;
     const int64_t j = (int64_t)blockIdx.x * kMaskTiles + w;  // vocabulary tile
     if (j >= nVt) break;
     bool k = false;
@@ -131,7 +143,7 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
     for (int u = 0; u < kRowsPerLane; ++u) {
       if (live[u]) {
         const bool hit = tl[u] >= j * kStatTile && tl[u] < (j + 1) * kStatTile && tl[u] < V;
-        k = k || no_filter || hit || (tm[u][j * N] - L[u] >= log_eps);
+        k = k || no_filter || hit || (x[q][u] - L[u] >= log_eps);
       }
     }
     k = __any_sync(0xffffffffu, k);

@@ -209,6 +209,30 @@ def test_ragged_shapes(N, D, V, dtype):
     check(run(e, c, t), oracle(e, c, t), dtype)
 
 
+def test_multichunk_fp16_bias_ragged():
+    """N = 4200 rows (not a multiple of 128) makes the backward take 16384-row
+    vocabulary chunks: V = 36000 gives three (the last one 3232 rows, not a
+    multiple of 64), so grad_e's two accumulator slabs are stored, then
+    reduce-added, and grad_c's MN-major operand falls back to 2-D boxes in the
+    last chunk.  fp16 with an fp32 bias, 10% ignored rows, reduction 'sum'.
+    Against the float64 oracle: the loss over all rows, dE on sampled rows, dC
+    and dBias on sampled vocabulary rows (both ends of every chunk)."""
+    e, c, t, b = small(4200, 128, 36000, torch.float16, seed=11, bias=torch.float32, ignore=0.1)
+    got = run(e, c, t, bias=b, reduction="sum")
+    en, cn, bn = e.numpy(), c.numpy(), b.numpy()
+    safe, valid = O.sanitize(t.numpy())
+    lse, tgt = O.rows_lse_tgt(en, cn, safe, np.arange(4200), bias=bn, chunk=4096)
+    np.testing.assert_allclose(got["loss"], ((lse - tgt) * valid).sum(), rtol=LOSS_RTOL[torch.float16])
+    d = O.d_nll_from_reduction(valid, "sum")
+    rows = np.array([0, 1, 127, 128, 2048, 4095, 4096, 4199])
+    dE = O.rows_grad_e(en, cn, safe, lse[rows], d[rows], rows, bias=bn)
+    cols = np.array([0, 63, 64, 16383, 16384, 32767, 32768, 35999])
+    dC, dB = O.cols_grad_c(en, cn, safe, lse, d, cols, bias=bn)
+    assert O.rel_max_abs(got["dE"][rows], dE) < GRAD_TOL
+    assert O.rel_max_abs(got["dC"][cols], dC) < GRAD_TOL
+    assert O.rel_max_abs(got["dB"][cols], dB) < GRAD_TOL
+
+
 def test_empty_batch():
     dev = _dev()
     e = torch.zeros(0, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
