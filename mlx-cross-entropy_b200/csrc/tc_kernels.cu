@@ -2,11 +2,13 @@
 //
 // One persistent, warp-specialised GEMM engine drives four epilogues:
 //
-//   K1 forward : S = e @ c^T per (128-row, 256-column) tile; the epilogue keeps
-//                an online max / sum-exp per row over each 128-column half,
-//                picks the target logit and adds the bias.  Replaces the tile
-//                kernel of csrc/cce/cce.metal:19-135 (which does the same per
-//                32x32 tile on 8x8 simdgroup MMAs).
+//   K1 forward : S = e @ c^T per (128-row, 256-column) tile; the epilogue adds
+//                the bias, picks the target logit, writes each row's max over
+//                every 32-column statistics tile (the backward filter's input)
+//                and one online (max, sum-exp) pair per row for the whole tile
+//                (the LSE partial).  Replaces the tile kernel of
+//                csrc/cce/cce.metal:19-135 (which does the same per 32x32 tile
+//                on 8x8 simdgroup MMAs).
 //   K4 dlogits : the same S for one vocabulary chunk, then
 //                w = d_nll * (exp(S + b - lse) - [v == t]) stored as bf16
 //                (cce.metal:274-282), with blocks the filter rejects
@@ -15,13 +17,23 @@
 //   K6 grad_c  : grad_c[chunk, D] = w^T @ e                    (cce.metal:292-304,
 //                reference/_fused_backward.py:1549-1567)
 //
-// Engine: 192 threads, one CTA per SM, grid = min(#tiles, #SMs), static
-// round-robin tile schedule.  Warp 0 lane 0 issues TMA loads of the A and B
-// K-slices (64 elements = one 128-byte swizzle row) into a 4-stage ring; warp 1
-// lane 0 issues tcgen05.mma (M=128, N=256, K=16) into one of two 256-column
-// fp32 TMEM accumulators and commits stage / accumulator barriers; warps 2-5
-// read the accumulator with tcgen05.ld (one TMEM lane = one output row per
-// thread) and run the epilogue while the next tile's MMAs proceed.
+// Engine: 192 threads, one CTA per SM, grid = min(#work units, #SMs).  Warp 0
+// lane 0 takes work units (a tile, or a tile's K range for grad_e) from a
+// static round-robin schedule (forward) or a global atomic counter (backward)
+// and issues the TMA loads of the A and B K-slices (64 elements = one 128-byte
+// swizzle row) into a 4-stage ring, skipping the K-blocks the filter rejects;
+// warp 1 lane 0 issues tcgen05.mma (M=128, N=256 or fewer, K=16) into one of
+// two 256-column fp32 TMEM accumulators and commits stage / accumulator
+// barriers; warps 2-5 read the accumulator with tcgen05.ld (one TMEM lane =
+// one output row per thread) and run the epilogue, which leaves through TMA
+// box stores, while the next tile's MMAs proceed.
+//
+// An epilogue type supplies: kMask (reads a filter-mask slice) and, if so,
+// kMaskBits (the slice is already a bit table) with mask_src / mask_ld /
+// mask_rows / mask_cols; tile_active, next_kb and ksub_mask (which tiles,
+// K-blocks and K=16 steps run); col_mask (the column groups the MMA computes,
+// K-major B only); chunk_live (which 32-column chunks the epilogue reads from
+// TMEM); begin / chunk / end (per tile, per 32-column chunk, per tile end).
 #include <cuda.h>
 
 #include <atomic>
@@ -117,10 +129,6 @@ struct MaskView {
   int64_t ld;
   int wpr;
   int cols;
-  __device__ __forceinline__ bool get(int r, int c) const {
-    if (bits) return (bits[r * wpr + (c >> 5)] >> (c & 31)) & 1u;
-    return bytes[(int64_t)r * ld + c] != 0;
-  }
   // Bits [c, c + n) of row r (n <= 32 divides 32, c a multiple of n).
   __device__ __forceinline__ uint32_t field(int r, int c, int n) const {
     const uint32_t lo = n == 32 ? 0xffffffffu : (1u << n) - 1u;
@@ -274,7 +282,6 @@ struct FwdEpi {
   static constexpr bool kMask = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
   __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
-  static constexpr bool kMaskBits = false;
   __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
   __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
@@ -459,7 +466,6 @@ struct GradEEpi {
   // steps of the rejected ones.
   static constexpr bool kMask = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
-  __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
   static constexpr bool kMaskBits = false;
   static constexpr int kSpk = BK / kStatTile;  // statistics tiles per K-block
   // K=16 steps of K-block kb whose statistics tile the filter keeps (kb active).
