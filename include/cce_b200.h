@@ -188,6 +188,24 @@ CCE_API int cce_backward(const void* e, const void* c, const void* bias, int bia
                  void* grad_e, void* grad_c, float* grad_bias, int64_t* skip_stats,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * cce_dequantize -- expand rows of an affine group-quantised classifier.
+ *
+ * No counterpart in the reference's library: its mlx-lm recipe dequantises
+ * the whole [V, D] head with MLX before every call (README.md:84-95).  The
+ * quantised layout is MLX's affine one for bits in {2, 4, 8}:
+ *   wq     [rows][D * bits / 32] uint32: 32 / bits values per word, value j
+ *          of a row in bits [(j * bits) % 32, +bits) of word (j * bits) / 32
+ *   scales, biases [rows][D / group_size] in scale_dtype (F32 / F16 / BF16)
+ *   out[r][j] = scales[r][j / group_size] * q + biases[r][j / group_size],
+ *          written in out_dtype (F32 / F16 / BF16), [rows][D] row-major.
+ * group_size in {32, 64, 128}, D a multiple of group_size.  Pass the first
+ * row's pointers to expand a range of rows (a vocabulary chunk).
+ */
+CCE_API int cce_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scale_dtype,
+                           int64_t rows, int64_t D, int group_size, int bits, int out_dtype, void* out,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -304,6 +304,67 @@ cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype
   return launched();
 }
 
+// Affine group dequantisation: one thread per packed word, its 32 / BITS values
+// share one group (group_size >= 32 >= 32 / BITS), so one scale and bias.
+template <int BITS, typename TS, typename TO>
+__global__ void dequant_kernel(const uint32_t* __restrict__ wq, const TS* __restrict__ scales,
+                               const TS* __restrict__ biases, int64_t words, int64_t wpr, int64_t gpr,
+                               int group, TO* __restrict__ out) {
+  constexpr int kPer = 32 / BITS;
+  constexpr uint32_t kMask = (1u << BITS) - 1u;
+  for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = w / wpr;
+    const int64_t j0 = (w - r * wpr) * kPer;  // first value of the word within the row
+    const int64_t g = r * gpr + j0 / group;
+    const float s = to_f32(scales[g]), b = to_f32(biases[g]);
+    const uint32_t q = __ldg(wq + w);
+    TO* dst = out + r * (wpr * kPer) + j0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) dst[i] = from_f32<TO>(fmaf(s, (float)((q >> (i * BITS)) & kMask), b));
+  }
+}
+
+template <typename TS, typename TO>
+cudaError_t dequant_dispatch(const uint32_t* wq, const void* scales, const void* biases, int64_t rows,
+                             int64_t D, int group, int bits, void* out, cudaStream_t stream) {
+  const int64_t wpr = D * bits / 32, gpr = D / group, words = rows * wpr;
+  const int grid = grid_for(words, 256);
+  const TS* s = static_cast<const TS*>(scales);
+  const TS* b = static_cast<const TS*>(biases);
+  TO* o = static_cast<TO*>(out);
+  switch (bits) {
+    case 2: dequant_kernel<2, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
+    case 4: dequant_kernel<4, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
+    case 8: dequant_kernel<8, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return launched();
+}
+
+template <typename TS>
+cudaError_t dequant_out(const uint32_t* wq, const void* scales, const void* biases, int64_t rows, int64_t D,
+                        int group, int bits, int out_dtype, void* out, cudaStream_t stream) {
+  switch (out_dtype) {
+    case CCE_F32: return dequant_dispatch<TS, float>(wq, scales, biases, rows, D, group, bits, out, stream);
+    case CCE_F16: return dequant_dispatch<TS, __half>(wq, scales, biases, rows, D, group, bits, out, stream);
+    case CCE_BF16: return dequant_dispatch<TS, __nv_bfloat16>(wq, scales, biases, rows, D, group, bits, out, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scale_dtype,
+                              int64_t rows, int64_t D, int group, int bits, int out_dtype, void* out,
+                              cudaStream_t stream) {
+  if (rows == 0 || D == 0) return cudaSuccess;
+  switch (scale_dtype) {
+    case CCE_F32: return dequant_out<float>(wq, scales, biases, rows, D, group, bits, out_dtype, out, stream);
+    case CCE_F16: return dequant_out<__half>(wq, scales, biases, rows, D, group, bits, out_dtype, out, stream);
+    case CCE_BF16: return dequant_out<__nv_bfloat16>(wq, scales, biases, rows, D, group, bits, out_dtype, out, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream) {
   pow2_absmax_kernel<<<1, 1024, 0, stream>>>(x, n, out);
   return launched();

@@ -391,4 +391,24 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   return CCE_OK;
 }
 
+int cce_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scale_dtype, int64_t rows,
+                   int64_t D, int group_size, int bits, int out_dtype, void* out, void* stream) {
+  if (rows < 0 || D < 0) return fail(CCE_ERR_SHAPE, "cce_dequantize: negative size");
+  if (bits != 2 && bits != 4 && bits != 8) return fail(CCE_ERR_ARG, "cce_dequantize: bits must be 2, 4 or 8, got %d", bits);
+  if (group_size != 32 && group_size != 64 && group_size != 128)
+    return fail(CCE_ERR_ARG, "cce_dequantize: group_size must be 32, 64 or 128, got %d", group_size);
+  if (D % group_size != 0)
+    return fail(CCE_ERR_SHAPE, "cce_dequantize: D=%lld is not a multiple of group_size=%d", (long long)D, group_size);
+  if (!dtype_ok(scale_dtype) || !dtype_ok(out_dtype))
+    return fail(CCE_ERR_DTYPE, "cce_dequantize: dtype codes %d / %d", scale_dtype, out_dtype);
+  if (rows == 0 || D == 0) return CCE_OK;
+  if (!wq || !scales || !biases || !out) return fail(CCE_ERR_ARG, "cce_dequantize: NULL pointer");
+  int rc = check_arch();
+  if (rc) return rc;
+  CCE_CUDA_CHECK(cce::launch_dequantize(wq, scales, biases, scale_dtype, rows, D, group_size, bits, out_dtype, out,
+                                        (cudaStream_t)stream),
+                 "cce_dequantize");
+  return CCE_OK;
+}
+
 }  // extern "C"

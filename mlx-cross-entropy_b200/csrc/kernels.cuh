@@ -61,6 +61,10 @@ cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int
                               float log_eps, bool no_filter, uint8_t* keep, uint32_t* keep_t,
                               int64_t keep_t_ld, int64_t* skip_stats, cudaStream_t stream);
 cudaError_t launch_cast_f32(const float* src, void* dst, int dtype, int64_t n, cudaStream_t stream);
+// out[r][j] = scales[r][j / group] * q[r][j] + biases[r][j / group]  (cce_dequantize)
+cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scale_dtype,
+                              int64_t rows, int64_t D, int group, int bits, int out_dtype, void* out,
+                              cudaStream_t stream);
 // dst[i] = a[i] + b[i], written in dtype (CCE_F32 / F16 / BF16)
 cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype, int64_t n, cudaStream_t stream);
 // out[0] = s = the power of two >= max |x| (1 if all zero), out[1] = 1 / s

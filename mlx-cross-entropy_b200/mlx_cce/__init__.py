@@ -11,7 +11,9 @@ the flat ``cce_loss`` and the one-call ``cut_cross_entropy``, with
 (float32, float16 or bfloat16) instead of MLX arrays; the loss is float32.
 The [N, V] logits are never materialised.  The research package's extras
 ``shift`` and ``return_lse`` (reference/__init__.py:22-57) and the
-``LinearCrossEntropy`` module (reference/__init__.py:88-118) are provided too.
+``LinearCrossEntropy`` module (reference/__init__.py:88-118) are provided too,
+and ``linear_cross_entropy_quantized`` for an affine group-quantised head
+(the reference's mlx-lm recipe dequantises the whole head first, README.md:84-95).
 
 Kernels: hand-written sm_100a CUDA in ``libcce_b200.so`` (tcgen05 / TMEM / TMA
 for 16-bit inputs, CUDA-core FFMA for float32), called through its C ABI.
@@ -28,7 +30,8 @@ from ._autograd import REDUCTIONS, CCEFunction, sanitize_targets
 from ._ext import FILTER_LOG_EPS, cce_backward_raw, cce_forward_raw, cut_cross_entropy
 
 __all__ = ["linear_cross_entropy", "cce_loss", "cut_cross_entropy", "LinearCrossEntropy",
-           "cce_forward_raw", "cce_backward_raw", "FILTER_LOG_EPS"]
+           "cce_forward_raw", "cce_backward_raw", "FILTER_LOG_EPS", "QuantizedClassifier",
+           "linear_cross_entropy_quantized"]
 
 
 def _cce(e, c, targets, bias, reduction, ignore_index, filter_log_eps, group, v_offset,
@@ -108,3 +111,6 @@ class LinearCrossEntropy(torch.nn.Module):
     def forward(self, e, c, targets, bias=None):
         return linear_cross_entropy(e, c, targets, bias=bias, reduction=self.reduction,
                                     ignore_index=self.ignore_index, shift=self.shift)
+
+
+from .quantized import QuantizedClassifier, linear_cross_entropy_quantized  # noqa: E402

@@ -49,7 +49,7 @@ FILTER_LOG_EPS = math.log(2.0 ** -12)
 EXPORTED_SYMBOLS = (
     "cce_version", "cce_last_error", "cce_launch_count", "cce_device_status", "cce_num_stat_tiles",
     "cce_forward_workspace_bytes", "cce_forward", "cce_forward_noalloc", "cce_lse_combine",
-    "cce_backward_workspace_bytes", "cce_backward",
+    "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize",
 )
 
 _DTYPE_CODE = {torch.float32: CCE_F32, torch.float16: CCE_F16, torch.bfloat16: CCE_BF16}
@@ -89,6 +89,8 @@ def _load():
     lib.cce_backward.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_int, c_int, c_f, c_vp, c_vp, c_vp, c_vp, c_vp,
                                  c_sz, c_vp]
+    lib.cce_dequantize.restype = c_int
+    lib.cce_dequantize.argtypes = [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_vp]
     return lib
 
 
@@ -309,6 +311,36 @@ def backward(e, c, targets, lse, d_nll, tile_max, bias=None, *, v_offset: int = 
     return grad_e, grad_c, grad_b
 
 
+def dequantize(wq, scales, biases, group_size: int, bits: int, dtype, out=None, stream=None):
+    """Expand rows of an affine group-quantised matrix (``cce_dequantize``).
+
+    wq uint32 [rows, D * bits / 32] (32 / bits values per word, low bits
+    first; torch.int32 storage is accepted as the same bits), scales / biases
+    [rows, D / group_size]; returns ``scales * q + biases`` as ``dtype``
+    [rows, D] (into ``out`` when given).
+    """
+    what = "cce_dequantize"
+    if wq.dim() != 2 or scales.dim() != 2 or biases.shape != scales.shape:
+        raise ValueError(f"[{what}] wq must be 2D and scales / biases 2D of equal shape")
+    if wq.dtype not in (torch.int32, torch.uint32):
+        raise ValueError(f"[{what}] wq must hold 32-bit words, got {wq.dtype}")
+    if bits not in (2, 4, 8):
+        raise ValueError(f"[{what}] bits must be 2, 4 or 8, got {bits}")
+    rows = wq.shape[0]
+    D = wq.shape[1] * 32 // bits
+    if scales.shape != (rows, D // group_size):
+        raise ValueError(f"[{what}] scales must be [{rows}, {D // group_size}], got {tuple(scales.shape)}")
+    dev = _require_cuda(what, wq=wq, scales=scales, biases=biases)
+    if out is None:
+        out = torch.empty((rows, D), dtype=dtype, device=dev)
+    elif out.shape != (rows, D) or out.dtype != dtype or not out.is_contiguous():
+        raise ValueError(f"[{what}] out must be a contiguous [{rows}, {D}] {dtype} tensor")
+    rc = lib.cce_dequantize(_ptr(wq), _ptr(scales), _ptr(biases), dtype_code(scales.dtype, what), rows, D,
+                            int(group_size), int(bits), dtype_code(dtype, what), _ptr(out), _stream(stream))
+    _check(rc, what)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # The reference's three module-level entry points (csrc/bindings.cpp:15-86).
 # ---------------------------------------------------------------------------
@@ -321,9 +353,10 @@ def cce_forward_raw(e, c, targets, bias=None, *, stream=None):
     """Mirror of ``cce_forward_raw`` (csrc/bindings.cpp:58-69, cce.cpp:123-145).
 
     Returns ``[tile_max_flat, tile_sum_exp_flat, neg_target_logit, lse]`` like
-    the reference, except that the tile statistics cover 64-column tiles in
-    tile-major order (``[ceil(V/64) * N]``) and ``tile_sum_exp`` is not kept
-    (it is folded into ``lse`` on the device), so an empty tensor stands in.
+    the reference, except that the 32-column tile maxima are in tile-major
+    order (``[ceil(V/32) * N]``, the reference's is row-major) and
+    ``tile_sum_exp`` is not kept (it is folded into ``lse`` on the device), so
+    an empty tensor stands in.
     """
     tile_max, lse, tgt = forward(e, c, _as_i32_targets(targets), bias, stream=stream)
     return [tile_max.reshape(-1), tile_max.new_empty((0,)), -tgt, lse]

@@ -21,6 +21,13 @@ It restates, in numpy, the reference's pure-MLX implementation of the path:
   any row has its target in it or ``tile_max - lse >= ln(2^-12)``).
 * ``reduce``            -- mlx_cce/__init__.py:59-76 (sanitised targets,
   valid mask, none / sum / mean with the max(count, 1) denominator).
+* ``quantize_affine`` / ``dequantize_affine`` -- the affine group
+  quantisation the reference's mlx-lm recipe undoes before every call
+  (README.md:84-95, ``mx.dequantize`` of a quantised head): per group of
+  ``group_size`` values along D, w = scale * q + bias with q in
+  [0, 2^bits); q packed 32 / bits per uint32, low bits first.  The format is
+  MLX's (mlx.core.quantize, third-party, not vendored); this restates its
+  published definition for bits in {2, 4, 8}.
 
 PARITY UNPINNED: the reference's arithmetic lives in MLX (pinned only as
 ``mlx>=0.22.0``, pyproject.toml:5,18), which is not installed here and cannot
@@ -325,3 +332,47 @@ def cpu_fwd_bwd_step(e, c, targets, bias=None, reduction="mean", ignore_index=-1
         if dB is not None:
             dB[v0:v1] = p.sum(axis=0)
     return loss, dE, dC, dB
+
+
+# ---------------------------------------------------------------------------
+# Affine group quantisation of the classifier (see the module docstring).
+# ---------------------------------------------------------------------------
+
+def pack_words(q, bits):
+    """q int [rows, D] in [0, 2^bits) -> uint32 [rows, D * bits / 32], low bits first."""
+    q = np.asarray(q, dtype=np.uint64)
+    per = 32 // bits
+    rows, D = q.shape
+    qq = q.reshape(rows, D // per, per)
+    shifts = (np.arange(per, dtype=np.uint64) * bits)[None, None, :]
+    return (qq << shifts).sum(axis=2).astype(np.uint32)
+
+
+def unpack_words(wq, bits):
+    """Inverse of pack_words: uint32 [rows, W] -> int64 [rows, W * 32 / bits]."""
+    w = np.asarray(wq, dtype=np.uint64)
+    per = 32 // bits
+    shifts = (np.arange(per, dtype=np.uint64) * bits)[None, None, :]
+    q = (w[:, :, None] >> shifts) & np.uint64((1 << bits) - 1)
+    return q.reshape(w.shape[0], -1).astype(np.int64)
+
+
+def quantize_affine(w, group_size, bits):
+    """w [rows, D] -> (wq uint32, scales, biases) with w ~ scales * q + biases per group
+    (scale = (max - min) / (2^bits - 1), bias = min, q = round((w - bias) / scale))."""
+    w = np.asarray(w, dtype=np.float64)
+    rows, D = w.shape
+    g = w.reshape(rows, D // group_size, group_size)
+    lo, hi = g.min(axis=2), g.max(axis=2)
+    scale = (hi - lo) / ((1 << bits) - 1)
+    scale = np.where(scale == 0, 1.0, scale)
+    q = np.clip(np.rint((g - lo[:, :, None]) / scale[:, :, None]), 0, (1 << bits) - 1).astype(np.int64)
+    return pack_words(q.reshape(rows, D), bits), scale, lo
+
+
+def dequantize_affine(wq, scales, biases, group_size, bits):
+    """uint32 [rows, D * bits / 32] + per-group scales / biases -> float64 [rows, D]."""
+    q = unpack_words(wq, bits).astype(np.float64)
+    s = np.repeat(np.asarray(scales, np.float64), group_size, axis=1)
+    b = np.repeat(np.asarray(biases, np.float64), group_size, axis=1)
+    return s * q + b
