@@ -86,6 +86,14 @@ CCE_API uint64_t cce_launch_count(void);
  * time out). */
 CCE_API int cce_device_status(int reset);
 
+/* Diagnostic of that failure path: launches one thread that waits on a
+ * pipeline barrier nothing completes, with a limit of limit_ns (at most 2 s);
+ * the wait runs out, records CCE_SELFTEST_WAIT_CODE in the device status
+ * word and returns, so cce_device_status then reports it and the context
+ * stays usable.  No fault, trap or hang is involved. */
+#define CCE_SELFTEST_WAIT_CODE 99
+CCE_API int cce_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* Number of vocabulary tile statistics per row: ceil(V / CCE_STAT_TILE). */
 CCE_API int64_t cce_num_stat_tiles(int64_t V);
 

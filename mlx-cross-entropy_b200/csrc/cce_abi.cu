@@ -210,6 +210,16 @@ int cce_device_status(int reset) {
   return CCE_OK;
 }
 
+int cce_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > 2000000000ll)
+    return fail(CCE_ERR_ARG, "cce_selftest_wait_timeout: limit_ns must be in (0, 2e9], got %lld", (long long)limit_ns);
+  int rc = check_arch();
+  if (rc) return rc;
+  CCE_CUDA_CHECK(cce::tc_selftest_wait((uint64_t)limit_ns, CCE_SELFTEST_WAIT_CODE, (cudaStream_t)stream),
+                 "cce_selftest_wait_timeout");
+  return CCE_OK;
+}
+
 int64_t cce_num_stat_tiles(int64_t V) { return V <= 0 ? 0 : cce::ceil_div(V, cce::kStatTile); }
 
 // The LSE partials (max, sum-exp) per row per kernel tile: 2 x ceil(V / 128) x N

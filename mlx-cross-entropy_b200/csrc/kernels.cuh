@@ -95,5 +95,7 @@ cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
 // acc2[0] + acc2[1] after the last chunk (launch_sum2_f32).
 cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t stream);
 cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
+// one bounded pipeline wait that nothing satisfies: records `code` after limit_ns
+cudaError_t tc_selftest_wait(uint64_t limit_ns, int code, cudaStream_t stream);
 
 }  // namespace cce

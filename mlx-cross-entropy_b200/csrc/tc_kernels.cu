@@ -1461,6 +1461,28 @@ cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   return cudaErrorNotSupported;
 }
 
+namespace {
+
+// Diagnostic: one thread waits on a fresh mbarrier whose phase nothing
+// completes, so the bounded wait runs out after limit_ns, records `code` in
+// the status word and returns -- the path every pipeline wait takes when an
+// arrival is lost.
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int code) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    (void)mbar_wait(&bar, 0, code, limit_ns);
+  }
+}
+
+}  // namespace
+
+cudaError_t tc_selftest_wait(uint64_t limit_ns, int code, cudaStream_t s) {
+  selftest_wait_kernel<<<1, 32, 0, s>>>(limit_ns, code);
+  return launched();
+}
+
 int tc_read_status(bool reset) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_status, sizeof(int)) != cudaSuccess) return -1;

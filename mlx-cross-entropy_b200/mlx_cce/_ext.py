@@ -49,7 +49,7 @@ FILTER_LOG_EPS = math.log(2.0 ** -12)
 EXPORTED_SYMBOLS = (
     "cce_version", "cce_last_error", "cce_launch_count", "cce_device_status", "cce_num_stat_tiles",
     "cce_forward_workspace_bytes", "cce_forward", "cce_forward_noalloc", "cce_lse_combine",
-    "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize",
+    "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize", "cce_selftest_wait_timeout",
 )
 
 _DTYPE_CODE = {torch.float32: CCE_F32, torch.float16: CCE_F16, torch.bfloat16: CCE_BF16}
@@ -89,6 +89,8 @@ def _load():
     lib.cce_backward.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_int, c_int, c_f, c_vp, c_vp, c_vp, c_vp, c_vp,
                                  c_sz, c_vp]
+    lib.cce_selftest_wait_timeout.restype = c_int
+    lib.cce_selftest_wait_timeout.argtypes = [c_i64, c_vp]
     lib.cce_dequantize.restype = c_int
     lib.cce_dequantize.argtypes = [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_vp]
     return lib
