@@ -280,6 +280,7 @@ struct FwdEpi {
   };
 
   static constexpr bool kMask = false;
+  static constexpr bool kZeroTiles = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
   __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
   __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
@@ -370,6 +371,7 @@ struct DlogitsEpi {
 
   // The tile's four 64-column groups are the chunk's stat tiles 4 nb .. 4 nb + 3.
   static constexpr bool kMask = true;
+  static constexpr bool kZeroTiles = false;
   // Kept 64-column groups of the tile (bit g = chunk stat tile 4 nb + g).
   __device__ __forceinline__ uint32_t group_mask(const MaskView& mk, int mb, int nb) const {
     return mb < mask_rows ? mk.field(mb, kGroups * nb, kGroups) : 0u;
@@ -454,6 +456,8 @@ struct GradEEpi {
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
   int accumulate;
+  float* acc2;              // [2][N][D]: zero tiles of the first chunk are stored directly
+  int64_t N, D;
 
   struct State {
     int64_t col0;
@@ -461,10 +465,24 @@ struct GradEEpi {
     int y0;  // first row of this warp's 32-row slab
     int ks;  // accumulator slab
   };
+  // A work unit no K-block reached adds zeros: nothing to do after the first
+  // chunk; in the first chunk its slab rows are zeroed (lane l: 8 columns).
+  __device__ __forceinline__ void zero_tile(const State& st) const {
+    if (accumulate) return;
+    const int64_t c0 = st.col0 + 8 * (threadIdx.x & 31);
+    if (c0 >= D) return;
+    float* base = acc2 + (int64_t)st.ks * N * D + c0;
+    for (int i = 0; i < 32 && (int64_t)st.y0 + i < N; ++i) {
+      float4* dst = reinterpret_cast<float4*>(base + ((int64_t)st.y0 + i) * D);
+      dst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      dst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   // K runs over the chunk's vocabulary rows: K-block kb (64 rows) holds the
   // chunk's statistics tiles BK / kStatTile * kb + i; the MMA skips the K=16
   // steps of the rejected ones.
   static constexpr bool kMask = true;
+  static constexpr bool kZeroTiles = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
   static constexpr bool kMaskBits = false;
   static constexpr int kSpk = BK / kStatTile;  // statistics tiles per K-block
@@ -522,6 +540,7 @@ struct GradCEpi {
   // M tile mb covers the chunk's statistics tiles kStatsPerM * mb + i; K-block
   // kb (64 rows) lies in row block kb / 2.
   static constexpr bool kMask = true;
+  static constexpr bool kZeroTiles = true;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
   __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
   // The mask view is the transposed activity table: row = the chunk's 128-row
@@ -537,6 +556,13 @@ struct GradCEpi {
     return max(kb, r * kKpr);
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  // A tile no K-block reached is zero: lane l stores 8 columns of each row.
+  __device__ __forceinline__ void zero_tile(const State& st) const {
+    const int64_t c0 = st.col0 + 8 * (threadIdx.x & 31);
+    if (c0 >= D) return;
+    for (int i = 0; i < 32 && (int64_t)st.y0 + i < rows; ++i)
+      *reinterpret_cast<uint4*>(out + ((int64_t)st.y0 + i) * D + c0) = make_uint4(0u, 0u, 0u, 0u);
+  }
   template <class S>
   __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
   __device__ __forceinline__ void begin(State& st, const MaskView&, int mb, int nb, int r, int) const {
@@ -565,7 +591,6 @@ struct GradCEpi {
 template <class Epi>
 __device__ __forceinline__ void load_mask_view(const Epi& epi, uint8_t* smask, MaskView& mk) {
   if constexpr (Epi::kMask) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows = epi.mask_rows, cols = epi.mask_cols;
     const int wpr = (cols + 31) / 32;
     const bool fits = (int64_t)rows * wpr * 4 <= SMASK_BYTES;
@@ -585,13 +610,18 @@ __device__ __forceinline__ void load_mask_view(const Epi& epi, uint8_t* smask, M
     } else {
       const uint8_t* src0 = static_cast<const uint8_t*>(epi.mask_src);
       if (fits) {
-        for (int rr = warp; rr < rows; rr += blockDim.x / 32) {
-          const uint8_t* src = src0 + (int64_t)rr * epi.mask_ld;
-          for (int c0 = 0; c0 < cols; c0 += 32) {
-            const int cc = c0 + lane;
-            const uint32_t word = __ballot_sync(0xffffffffu, cc < cols && __ldg(src + cc) != 0);
-            if (lane == 0) sb[rr * wpr + (c0 >> 5)] = word;
-          }
+        // one thread per 32-column word, its 32 byte loads independent (a
+        // warp-wide ballot per word serialised ~100 L2 round trips per warp
+        // before the first tile)
+        for (int i = threadIdx.x; i < rows * wpr; i += blockDim.x) {
+          const int rr = i / wpr, w = i - rr * wpr;
+          const uint8_t* src = src0 + (int64_t)rr * epi.mask_ld + w * 32;
+          const int n = min(32, cols - w * 32);
+          uint32_t word = 0;
+#pragma unroll
+          for (int b = 0; b < 32; ++b)
+            if (b < n && __ldg(src + b) != 0) word |= 1u << b;
+          sb[i] = word;
         }
         mk.bits = sb;
         mk.wpr = wpr;
@@ -815,17 +845,25 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       typename Epi::State st;
       epi.begin(st, mk, mb, nb, r, ks);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      // a tile no K-block reached is all zeros: plain coalesced zero stores
+      // (or nothing, when zeros would be added), not the staged path
+      bool zero_tile = false;
+      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb;
+      if (zero_tile) {
+        if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        __syncwarp();
-        if (any_kb && epi.chunk_live(st, c)) {
-          tmem_ld32(tbase + c * 32, v);
-        } else {
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          if (any_kb && epi.chunk_live(st, c)) {
+            tmem_ld32(tbase + c * 32, v);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          epi.chunk(st, c, v, sg);
         }
-        epi.chunk(st, c, v, sg);
       }
       epi.end(st);
       __syncwarp();
@@ -1097,17 +1135,25 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       typename Epi::State st;
       epi.begin(st, mk, vmb, nb, r, ks);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      // a tile no K-block reached is all zeros: plain coalesced zero stores
+      // (or nothing, when zeros would be added), not the staged path
+      bool zero_tile = false;
+      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb;
+      if (zero_tile) {
+        if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        __syncwarp();
-        if (any_kb && epi.chunk_live(st, c)) {
-          tmem_ld32(tbase + c * 32, v);
-        } else {
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          if (any_kb && epi.chunk_live(st, c)) {
+            tmem_ld32(tbase + c * 32, v);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          epi.chunk(st, c, v, sg);
         }
-        epi.chunk(st, c, v, sg);
       }
       epi.end(st);
       __syncwarp();
@@ -1419,7 +1465,7 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
   Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
            a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2), 2};
   GradEEpi epi{a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile), (int)ceil_div(a.N, kRowBlock),
-               (int)ceil_div(a.vc_len, kStatTile), accumulate ? 1 : 0};
+               (int)ceil_div(a.vc_len, kStatTile), accumulate ? 1 : 0, acc2, a.N, a.D};
   if (pair) return launch_gemm2<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
