@@ -6,7 +6,7 @@
 //   reduce_tile_to_lse of the reference (csrc/cce/cce.metal:332-355), with the
 //   target-logit sum and nll = lse - tgt (mlx_cce/__init__.py:32) fused in.
 // - block_mask_kernel: the reference's per-tile skip decision
-//   (csrc/cce/cce.metal:190-204) taken once per (128-row block, 64-column
+//   (csrc/cce/cce.metal:190-204) taken once per (128-row block, 32-column
 //   vocabulary tile) instead of inside the backward kernel.
 #include "kernels.cuh"
 

@@ -272,7 +272,7 @@ struct DlogitsEpi {
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
   int64_t N, V, v_offset, vc0, vc_end, ld;
-  // 1: every 64-column group of an active tile is written (the CTA-pair grad
+  // 1: every column group of an active tile is written (the CTA-pair grad
   // GEMMs read whole 256-row tiles); 0: only 128-column halves holding a kept
   // group (the single-CTA grad_c reads 128-row tiles, grad_e kept groups).
   int all_groups;
@@ -280,21 +280,21 @@ struct DlogitsEpi {
   struct State {
     int64_t row, tl, col0;
     float g, L, s;   // g = d_nll / s
-    uint32_t kmask;  // kept 64-column groups of the tile
+    uint32_t kmask;  // kept statistics-tile column groups of the tile
     int y0;          // first row of this warp's 32-row slab
   };
 
-  // The tile's four 64-column groups are the chunk's stat tiles 4 nb .. 4 nb + 3.
+  // The tile's kGroups column groups are the chunk's statistics tiles kGroups nb + g.
   static constexpr bool kMask = true;
   static constexpr bool kZeroTiles = false;
-  // Kept 64-column groups of the tile (bit g = chunk stat tile 4 nb + g).
+  // Kept column groups of the tile (bit g = chunk statistics tile kGroups nb + g).
   __device__ __forceinline__ uint32_t group_mask(const MaskView& mk, int mb, int nb) const {
     return mb < mask_rows ? mk.field(mb, kGroups * nb, kGroups) : 0u;
   }
   __device__ __forceinline__ bool tile_active(const MaskView& mk, int mb, int nb) const {
     return group_mask(mk, mb, nb) != 0;
   }
-  // 64-column groups the MMA computes: only the kept ones (the epilogue never
+  // Column groups the MMA computes: only the kept ones (the epilogue never
   // reads the accumulator columns of the others).
   __device__ __forceinline__ uint32_t col_mask(const MaskView& mk, int mb, int nb) const {
     return all_groups ? kAllGroups : group_mask(mk, mb, nb);
