@@ -334,11 +334,14 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         stepc, sample, cores, _ = cpu_reference_step_fn(args.config, args.ref_rows)
         stepc()  # warm-up
-        t0 = time.perf_counter()
-        stepc()
-        dtc = time.perf_counter() - t0
+        runs = []
+        for _ in range(3):  # median of three
+            t0 = time.perf_counter()
+            stepc()
+            runs.append(time.perf_counter() - t0)
+        dtc = statistics.median(runs)
         cpu = {"value": args.ref_rows / dtc, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": sample}
+               "sample": sample + "; median of 3 runs after 1 warm-up"}
 
     if world > 1:
         dist.barrier()
