@@ -186,3 +186,47 @@ def test_synthetic_workloads_shapes_and_determinism():
     e4, c4, t4, b4, go4, w4 = synthetic.make_inputs(4, N=400, V=3000, D=32)
     assert b4 is not None and b4.dtype == torch.float32 and go4.shape == (400,)
     assert int((t4 == -100).sum()) == 100
+
+
+# --- property-based: random shapes, ignore patterns, reductions, bias ---
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=40, deadline=None)
+@given(N=st.integers(1, 24), D=st.integers(1, 20), V=st.integers(1, 300),
+       reduction=st.sampled_from(["none", "sum", "mean"]), bias=st.booleans(),
+       ignore_frac=st.sampled_from([0.0, 0.3, 1.0]), seed=st.integers(0, 10_000))
+def test_oracle_matches_torch_on_random_shapes(N, D, V, reduction, bias, ignore_frac, seed):
+    """Loss, dE, dC and dBias of the oracle equal torch's F.cross_entropy +
+    autograd (float64) for any shape, including fully ignored batches."""
+    e, c, t, b = _inputs(N, D, V, seed=seed, scale=0.5, bias=bias)
+    g = torch.Generator().manual_seed(seed + 1)
+    t[torch.rand(N, generator=g) < ignore_frac] = -100
+    e.requires_grad_(True)
+    c.requires_grad_(True)
+    if b is not None:
+        b.requires_grad_(True)
+    out = _torch_loss(e, c, t, b, reduction)
+    go = torch.randn(out.shape, dtype=torch.float64, generator=g) if reduction == "none" else None
+    if (t == -100).all() and reduction == "mean":
+        # torch returns nan for an all-ignored mean; the reference divides by max(count, 1)
+        loss, _lse, dE, dC, dB = O.loss_and_grads(e.detach().numpy(), c.detach().numpy(), t.numpy(),
+                                                  None if b is None else b.detach().numpy(), reduction)
+        assert loss == 0.0 and not np.any(dE) and not np.any(dC)
+        return
+    (out.backward(go) if go is not None else out.backward())
+    loss, _lse, dE, dC, dB = O.loss_and_grads(
+        e.detach().numpy(), c.detach().numpy(), t.numpy(), None if b is None else b.detach().numpy(),
+        reduction, grad_out=None if go is None else go.numpy())
+    np.testing.assert_allclose(np.asarray(loss).reshape(-1), out.detach().numpy().reshape(-1),
+                               rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(dE, e.grad.numpy(), rtol=1e-9, atol=1e-12)
+    np.testing.assert_allclose(dC, c.grad.numpy(), rtol=1e-9, atol=1e-12)
+    if b is not None:
+        np.testing.assert_allclose(dB, b.grad.numpy(), rtol=1e-9, atol=1e-12)
+    nll_c, lse_c, _, _ = O.chunked_forward(e.detach().numpy(), c.detach().numpy(), t.numpy(),
+                                           None if b is None else b.detach().numpy(), chunk=37)
+    nll_d, lse_d, _, _ = O.dense_forward(e.detach().numpy(), c.detach().numpy(), t.numpy(),
+                                         None if b is None else b.detach().numpy())
+    np.testing.assert_allclose(lse_c, lse_d, rtol=1e-6, atol=1e-6)
