@@ -374,6 +374,8 @@ def run_ours(args, rank, world, local_rank):
             # whole-job TFLOP/s against the peak of all N GPUs together
             "tflops": tflops, "pct_bf16_peak": tflops / (peak_burst * world),
             "pct_bf16_peak_sustained": tflops / (peak_sus * world),
+            # against the 2.25 PFLOP/s dense-BF16 figure NVIDIA quotes per B200
+            "pct_bf16_spec": tflops / (2250.0 * world),
             "flops_per_step": flops,
             "skipped_blocks_frac": (skipped / total) if total else None,
             "fwd_ms": fwd_avg, "bwd_ms": bwd_avg,
