@@ -71,6 +71,9 @@ def test_error_codes_without_gpu_work():
     assert rc == _ext.CCE_ERR_ARG
     rc = lib.cce_lse_combine(None, None, 0, 4, 4, None, None, None, None)
     assert rc == _ext.CCE_ERR_SHAPE
+    # the bounded-wait self-test takes a limit in (0, 2 s]
+    assert lib.cce_selftest_wait_timeout(0, None) == _ext.CCE_ERR_ARG
+    assert lib.cce_selftest_wait_timeout(3_000_000_000, None) == _ext.CCE_ERR_ARG
 
 
 def test_python_api_rejects_cpu_tensors_and_bad_args():
