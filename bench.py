@@ -56,6 +56,40 @@ def forward_traffic_bytes(N, D, V_local):
     return 33.55e6 + (1168.373248e6 - 33.55e6) * V_local / 128256
 
 
+def load_synthetic():
+    """The workload generator, loaded from its file without importing the
+    ``mlx_cce`` package (whose import loads the CUDA library): the reference
+    arm must map none of this repository's native code."""
+    import importlib.util
+    path = REPO / "mlx-cross-entropy_b200" / "mlx_cce" / "synthetic.py"
+    spec = importlib.util.spec_from_file_location("cce_synthetic", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["cce_synthetic"] = mod  # dataclasses resolve the module by name
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def workload_config(w, N, D, V, world, scaled):
+    """The ``config`` object of both arms' JSON lines (identical for one workload)."""
+    return {"workload": f"cfg{w.cfg} {w.name}" + (" (scaled)" if scaled else ""),
+            "N": N, "D": D, "V": V,
+            "global_batch": N, "seq_len": w.batch[-1] if len(w.batch) > 1 and not scaled else N,
+            "reduction": w.reduction,
+            "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (c is %.2f GB), no flush" % (V * D * 2 / 1e9)}
+
+
+def probe_mlx():
+    """Whether the reference's own array library imports here (it never has:
+    MLX targets Apple silicon and is not in this image).  Returns the outcome
+    as one line for the reference arm's note."""
+    try:
+        import mlx.core  # noqa: F401
+        return "import mlx.core succeeded"
+    except Exception as exc:  # ImportError / ModuleNotFoundError expected
+        return f"import mlx.core failed: {type(exc).__name__}: {exc}"
+
+
 def env_int(name, default):
     v = os.environ.get(name)
     return int(v) if v not in (None, "") else default
@@ -122,8 +156,9 @@ def cpu_reference_step_fn(cfg, rows):
     """Returns (step(), sample description, cores) timing the oracle on a row sample."""
     sys.path.insert(0, str(REPO))
     from oracle import cce_oracle as O
-    from mlx_cce import synthetic
+    synthetic = load_synthetic()
     e, c, t, bias, go, w = synthetic.make_inputs(cfg)
+    rows = min(rows, w.N)
     e2 = e.reshape(-1, w.D)[:rows].float().numpy()
     t2 = t.reshape(-1)[:rows].numpy()
     c32 = c.float().numpy()
@@ -140,7 +175,7 @@ def cpu_reference_step_fn(cfg, rows):
         cores = os.cpu_count() or 1
     sample = (f"first {rows} of {w.N} rows of config {cfg} against the full V={w.V} x D={w.D} "
               f"classifier: chunked online-LSE forward + analytic dE/dC backward, float32 numpy")
-    return step, sample, cores, w
+    return step, sample, cores, w, rows
 
 
 def run_reference(args, rank, world):
@@ -151,9 +186,9 @@ def run_reference(args, rank, world):
     from threadpoolctl import threadpool_limits
     ncpu = os.cpu_count() or 1
     torch.set_num_threads(ncpu)
+    mlx_note = probe_mlx()
     with threadpool_limits(limits=ncpu):
-        rows = args.ref_rows
-        step, sample, cores, w = cpu_reference_step_fn(args.config, rows)
+        step, sample, cores, w, rows = cpu_reference_step_fn(args.config, args.ref_rows)
         for _ in range(args.warmup):
             step()
         t0 = time.perf_counter()
@@ -166,16 +201,134 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": f"cfg{w.cfg} {w.name}", "N": w.N, "D": w.D, "V": w.V,
-                   "global_batch": w.N, "parallelism": "cpu"},
+        "config": workload_config(w, w.N, w.D, w.V, world, False),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "MLX is not installable here: the reference's pure-MLX path is timed through its "
-                "CPU restatement (oracle/cce_oracle.py).",
+        "note": (f"{mlx_note}; the reference's pure-MLX path (reference/_chunked.py + "
+                 "reference/_metal_backward.py) is therefore timed through its CPU restatement "
+                 "(oracle/cce_oracle.py) on a row sample of the same workload; tokens/s = sample "
+                 "rows / step time"),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------
+# parity of the benchmarked step (checker leg: reads the oracle's fixtures)
+# ---------------------------------------------------------------------------
+
+LOSS_RTOL_16 = 1e-3   # BASELINE's loss tolerance for 16-bit inputs (1e-5 for fp32)
+GRAD_TOL = 2e-2       # relative max-abs gradient tolerance
+
+
+def parity_block(w, scaled, loss, lse, e_grad, c_grad, e_dev, c_dev, b_dev, e_cpu, t_cpu, c_full,
+                 b_full, go_cpu, v0, v1, rank, world, dev):
+    """Loss and sampled gradients of one benchmarked step against the float64 oracle.
+
+    With a committed fixture (tests/golden/cfg{1..4}.npz, the oracle's
+    outputs on the same seeded inputs) the loss, the sampled grad_e rows and
+    the sampled grad_c vocabulary rows of this rank's shard are compared with
+    it.  Without one (config 5, scaled runs) the oracle runs here on sampled
+    rows: rank 0 checks the LSE and grad_e of 8 rows against the full
+    classifier (``c_full``, ``b_full``), every rank the grad_c of sampled vocabulary rows
+    of its shard (given the GPU's global LSE), and the loss is compared with
+    the reduction of (GPU LSE - target logit), the target logits recomputed
+    in float64.  Every rank takes the same collective steps; each error is the
+    maximum over ranks.
+    """
+    import numpy as np
+    import torch.distributed as dist
+    sys.path.insert(0, str(REPO))
+    from oracle import cce_oracle as O
+
+    def allreduce(vals, op):
+        tt = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tt, op=op)
+        return tt.tolist()
+
+    MAX = dist.ReduceOp.MAX if world > 1 else None
+    fixture = REPO / "tests" / "golden" / f"cfg{w.cfg}.npz"
+    safe, valid = O.sanitize(t_cpu.numpy())
+    got_loss = loss.detach().double().cpu().numpy().reshape(-1)
+    rtol_loss = 1e-5 if w.dtype == torch.float32 else LOSS_RTOL_16
+    if fixture.exists() and not scaled:
+        ref = np.load(fixture)
+        ref_loss = np.asarray(ref["loss"], np.float64).reshape(-1)
+        loss_rel = float(np.abs(got_loss - ref_loss).max() / max(np.abs(ref_loss).max(), 1e-30))
+        rows = ref["rows"]
+        de = e_grad[torch.as_tensor(rows, device=dev)].double().cpu().numpy()
+        de_rel = O.rel_max_abs(de, ref["dE_rows"])
+        cols = ref["cols"]
+        mine = (cols >= v0) & (cols < v1)
+        num = 0.0
+        if mine.any():
+            got = c_grad[torch.as_tensor(cols[mine] - v0, device=dev)].double().cpu().numpy()
+            num = float(np.abs(got - ref["dC_cols"][mine]).max())
+        den = float(np.abs(ref["dC_cols"]).max()) or 1.0
+        loss_rel, de_rel, num = allreduce([loss_rel, de_rel, num], MAX)
+        out = {"loss_rel": loss_rel, "dE_rel": de_rel, "dC_rel": num / den,
+               "rows": int(len(rows)), "cols": int(len(cols)),
+               "source": f"tests/golden/{fixture.name}: float64 oracle on the same seeded inputs"}
+    else:
+        gw = go_cpu.reshape(-1).double().numpy() if go_cpu is not None else np.ones(len(safe))
+        d_nll = valid * gw
+        if w.reduction == "mean":
+            d_nll = d_nll / max(valid.sum(), 1)
+        lse_g = lse.detach().double().cpu().numpy()
+        e32 = e_cpu.float().numpy()
+        rng = np.random.default_rng(1000 + w.cfg)
+        lse_rel = de_rel = 0.0
+        if rank == 0:
+            rows = np.sort(rng.choice(len(safe), 8, replace=False))
+            cf = c_full.float().numpy()
+            bf = None if b_full is None else b_full.float().numpy()
+            lse_ref, _ = O.rows_lse_tgt(e32, cf, safe, rows, bias=bf)
+            lse_rel = float(np.abs(lse_g[rows] - lse_ref).max() / np.abs(lse_ref).max())
+            de_ref = O.rows_grad_e(e32, cf, safe, lse_ref, d_nll[rows], rows, bias=bf)
+            de = e_grad[torch.as_tensor(rows, device=dev)].double().cpu().numpy()
+            de_rel = O.rel_max_abs(de, de_ref)
+        # target logits in float64: each rank adds those of its shard's targets
+        tl = safe - v0
+        on = np.nonzero((tl >= 0) & (tl < v1 - v0))[0]
+        tgt = torch.zeros(len(safe), dtype=torch.float64, device=dev)
+        if len(on):
+            r_on = torch.as_tensor(on, device=dev)
+            c_on = c_dev.detach()[torch.as_tensor(tl[on], device=dev)].double()
+            tgt[r_on] = (e_dev[r_on].double() * c_on).sum(dim=1)
+            if b_dev is not None:
+                tgt[r_on] += b_dev.detach()[torch.as_tensor(tl[on], device=dev)].double()
+        if world > 1:
+            dist.all_reduce(tgt, op=dist.ReduceOp.SUM)
+        ref_loss = O.reduce(lse_g - tgt.cpu().numpy(), valid, w.reduction)
+        ref_loss = np.asarray(ref_loss, np.float64).reshape(-1)
+        loss_rel = float(np.abs(got_loss - ref_loss).max() / max(np.abs(ref_loss).max(), 1e-30))
+        # grad_c on 6 sampled vocabulary rows of this shard plus 2 target rows in it
+        vr = v1 - v0
+        pick = rng.choice(vr, min(6, vr), replace=False) + v0
+        tgts = np.unique(safe[valid][(safe[valid] >= v0) & (safe[valid] < v1)])[:2]
+        cols = np.unique(np.concatenate([pick, tgts])).astype(np.int64)
+        c_sub = c_dev.detach()[torch.as_tensor(cols - v0, device=dev)].float().cpu().numpy()
+        tmap = np.full(len(safe), -1, np.int64)
+        for j, col in enumerate(cols):
+            tmap[safe == col] = j
+        b_sub = None
+        if b_dev is not None:
+            b_sub = b_dev.detach()[torch.as_tensor(cols - v0, device=dev)].float().cpu().numpy()
+        dc_ref, _ = O.cols_grad_c(e32, c_sub, tmap, lse_g, d_nll, np.arange(len(cols)),
+                                  bias=b_sub)
+        got = c_grad[torch.as_tensor(cols - v0, device=dev)].double().cpu().numpy()
+        num, den = float(np.abs(got - dc_ref).max()), float(np.abs(dc_ref).max())
+        loss_rel, lse_rel, de_rel, num, den = allreduce([loss_rel, lse_rel, de_rel, num, den], MAX)
+        out = {"loss_rel": loss_rel, "lse_rel": lse_rel, "dE_rel": de_rel,
+               "dC_rel": num / (den or 1.0), "rows": 8, "cols_per_rank": int(len(cols)),
+               "source": ("float64 oracle on sampled rows; loss = reduction of (GPU lse - float64 "
+                          "target logit), the GPU lse checked on the sampled rows")}
+    out["tol"] = {"loss_rel": rtol_loss, "grad_rel": GRAD_TOL}
+    out["ok"] = bool(out["loss_rel"] < rtol_loss and out["dE_rel"] < GRAD_TOL
+                     and out["dC_rel"] < GRAD_TOL and out.get("lse_rel", 0.0) < rtol_loss)
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -205,25 +358,31 @@ def run_ours(args, rank, world, local_rank):
     c = c_cpu[v0:v1].contiguous().to(dev).requires_grad_(True)
     bias = b_cpu[v0:v1].contiguous().to(dev).requires_grad_(True) if b_cpu is not None else None
     go = go_cpu.reshape(N).to(dev) if go_cpu is not None else None
+    # the parity leg's sampled oracle needs the whole classifier on rank 0
+    # when no fixture covers the workload
+    fixture = (REPO / "tests" / "golden" / f"cfg{w.cfg}.npz").exists() and not scaled
+    keep_full = not args.no_parity and not fixture and rank == 0
+    c_full = c_cpu if keep_full else None
+    b_full = b_cpu if keep_full else None
     del c_cpu
     skip = torch.zeros(2, dtype=torch.int64, device=dev)
 
-    def step(e_in, t_in):
+    def step(e_in, t_in, full=False):
         e_in = e_in.detach().requires_grad_(True)
         c.grad = None
         if bias is not None:
             bias.grad = None
         if world > 1:
-            loss = mdist.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
-                                              v_offset=v0, skip_stats=skip)
+            loss, lse = mdist.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
+                                                   v_offset=v0, skip_stats=skip, return_lse=True)
         else:
-            loss = mlx_cce.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
-                                                skip_stats=skip)
+            loss, lse = mlx_cce.linear_cross_entropy(e_in, c, t_in, bias, reduction=w.reduction,
+                                                     skip_stats=skip, return_lse=True)
         if w.reduction == "none":
             loss.backward(go)
         else:
             loss.backward()
-        return loss
+        return (loss, lse, e_in) if full else loss
 
     def barrier():
         if world > 1:
@@ -329,10 +488,19 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
     h2d = e_host.numel() * e_host.element_size() + t_host.numel() * t_host.element_size()
 
+    # ---- parity of the benchmarked step (every rank, every N) ----
+    parity = None
+    if not args.no_parity:
+        loss_p, lse_p, e_p = step(e, t, full=True)
+        torch.cuda.synchronize()
+        parity = parity_block(w, scaled, loss_p, lse_p, e_p.grad, c.grad, e, c, bias, e_cpu, t_cpu,
+                              c_full, b_full, go_cpu, v0, v1, rank, world, dev)
+        del loss_p, lse_p, e_p
+
     # ---- CPU baseline (rank 0 at N=1 only) ----
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        stepc, sample, cores, _ = cpu_reference_step_fn(args.config, args.ref_rows)
+        stepc, sample, cores, _, crow = cpu_reference_step_fn(args.config, args.cpu_rows)
         stepc()  # warm-up
         runs = []
         for _ in range(3):  # median of three
@@ -340,7 +508,7 @@ def run_ours(args, rank, world, local_rank):
             stepc()
             runs.append(time.perf_counter() - t0)
         dtc = statistics.median(runs)
-        cpu = {"value": args.ref_rows / dtc, "unit": "tokens/s", "cores": cores, "kind": "port",
+        cpu = {"value": crow / dtc, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": sample + "; median of 3 runs after 1 warm-up"}
 
     if world > 1:
@@ -365,12 +533,7 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else str(w.dtype),
             "data": "synthetic (seeded, see mlx_cce/synthetic.py)",
-            "config": {"workload": f"cfg{w.cfg} {w.name}" + (" (scaled)" if scaled else ""),
-                       "N": N, "D": D, "V": V,
-                       "global_batch": N, "seq_len": w.batch[-1] if len(w.batch) > 1 and not scaled else N,
-                       "reduction": w.reduction,
-                       "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (c is %.2f GB), no flush" % (V * D * 2 / 1e9)},
+            "config": workload_config(w, N, D, V, world, scaled),
             # whole-job TFLOP/s against the peak of all N GPUs together
             "tflops": tflops, "pct_bf16_peak": tflops / (peak_burst * world),
             "pct_bf16_peak_sustained": tflops / (peak_sus * world),
@@ -400,6 +563,8 @@ def run_ours(args, rank, world, local_rank):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
     # a graph holding NCCL calls must be released before the process group
     del graph
@@ -417,9 +582,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ref-rows", type=int, default=256,
-                    help="rows of the workload in one CPU-reference step")
+    ap.add_argument("--ref-rows", type=int, default=1024,
+                    help="rows of the workload in one step of the reference arm (--impl reference)")
+    ap.add_argument("--cpu-rows", type=int, default=256,
+                    help="rows of the workload in the cpu_baseline leg of our arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the check of one step against the float64 oracle")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of graph replays")
     ap.add_argument("--N", type=int, default=None, help="scaled-down rows (profiling captures)")
     ap.add_argument("--V", type=int, default=None, help="scaled-down vocabulary (profiling captures)")

@@ -139,9 +139,12 @@ CCE_API int cce_forward(const void* e, const void* c, const void* bias, int bias
  * runs.  It calls no cudaMalloc / cudaFree.
  *   - limit: 2 * ceil(V / 128) * N <= 8388608 (e.g. V = 128256, N <= 4185);
  *     larger calls return CCE_ERR_WORKSPACE and do nothing.
- *   - the first call on each device looks up the array's device address
- *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *   - the first call in each CUDA context (normally: per device, in the
+ *     device's primary context) looks up the array's device address with
+ *     cudaGetSymbolAddress, with that device current; make that first call
+ *     before any stream capture.  The address is cached per context id, so a
+ *     host running its own driver-API context, or one that reset the device,
+ *     gets the address that is valid in its current context.
  *   - all calls on a device share the array: calls that overlap on the GPU
  *     (different streams, or different host threads without ordering) race.
  *     Each call writes every partial it reads, so nothing carries over.

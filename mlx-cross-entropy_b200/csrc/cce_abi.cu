@@ -4,6 +4,8 @@
 // csrc/cce/cce.cpp:41-73 (returned as status codes instead of thrown
 // exceptions), output and zero-fill set-up of cce.cpp:243-246 and :316-340,
 // and the dtype-keyed kernel choice of cce.cpp:221-231, :300-310.
+#include <cuda.h>
+
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -19,6 +21,32 @@ std::atomic<uint64_t> g_launches{0};
 cudaError_t launched() {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
+}
+
+namespace {
+
+template <typename Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
+}  // namespace
+
+bool current_context_id(unsigned long long* id) {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static const GetCurrentFn get_cur = driver_fn<GetCurrentFn>("cuCtxGetCurrent");
+  static const GetIdFn get_id = driver_fn<GetIdFn>("cuCtxGetId");
+  if (!get_cur || !get_id) return false;
+  CUcontext ctx = nullptr;
+  if (get_cur(&ctx) != CUDA_SUCCESS) return false;
+  *id = 0;
+  if (ctx == nullptr) return true;
+  return get_id(ctx, id) == CUDA_SUCCESS;
 }
 
 }  // namespace cce
@@ -153,8 +181,12 @@ int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
 // Side streams of the tensor-core backward: grad_e and grad_c of one chunk run
 // concurrently (grad_e on the higher-priority stream, launched first), so
 // grad_c's CTAs take the SMs that grad_e's last partial wave leaves idle.
-// One set per (host thread, device); created on first use, never destroyed.
+// One set per (host thread, device), tagged with the CUDA context it was
+// created in: a set from another context (the host's own driver-API context,
+// or a primary context since reset) is replaced, not used.  Created on first
+// use, never destroyed (a replaced set is left to its context).
 struct SideStreams {
+  unsigned long long ctx_id = 0;
   cudaStream_t se = nullptr, sc = nullptr;
   cudaEvent_t start = nullptr, ev_l = nullptr, ev_e = nullptr, ev_c = nullptr;
 };
@@ -166,8 +198,10 @@ int side_streams(SideStreams** out) {
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(CCE_ERR_CUDA, "device ordinal %d out of range", dev);
+  unsigned long long ctx = 0;
+  if (!cce::current_context_id(&ctx)) return fail(CCE_ERR_CUDA, "could not read the current CUDA context");
   SideStreams& ss = g_side[dev];
-  if (ss.se == nullptr) {
+  if (ss.se == nullptr || ss.ctx_id != ctx) {
     int lo = 0, hi = 0;
     err = cudaDeviceGetStreamPriorityRange(&lo, &hi);
     if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetStreamPriorityRange");
@@ -179,6 +213,8 @@ int side_streams(SideStreams** out) {
         (err = cudaEventCreateWithFlags(&n.ev_e, cudaEventDisableTiming)) != cudaSuccess ||
         (err = cudaEventCreateWithFlags(&n.ev_c, cudaEventDisableTiming)) != cudaSuccess)
       return cuda_fail(err, "creating the backward side streams");
+    // creating them made a context current if none was
+    if (!cce::current_context_id(&n.ctx_id)) return fail(CCE_ERR_CUDA, "could not read the current CUDA context");
     ss = n;
   }
   *out = &ss;

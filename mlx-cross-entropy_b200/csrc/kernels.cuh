@@ -13,6 +13,13 @@ cudaError_t launched();
 // Records `msg` as this thread's cce_last_error() and returns `code`.
 int report_error(int code, const char* msg);
 
+// Process-unique id of the CUDA context current on this thread (cuCtxGetId);
+// *id = 0 when no context is current yet.  False if the driver calls fail.
+// Per-context host state (device addresses of symbols, streams) is keyed by
+// it: device ordinals are not enough once a host runs its own driver-API
+// context or resets a device.
+bool current_context_id(unsigned long long* id);
+
 struct FwdArgs {
   const void* e;
   const void* c;

@@ -12,11 +12,15 @@
 // The array is a file-scope __device__ symbol of kMaxScratchFloats floats
 // (32 MiB): every GPU that loads the library holds it until the process
 // exits, whether or not this entry point is used.  Host code cannot use the
-// symbol's name as a device address, so the address is looked up once per
-// device with cudaGetSymbolAddress (the set-up below) and passed to the
-// kernels as their workspace pointer.
-#include <atomic>
+// symbol's name as a device address, so the address is looked up with
+// cudaGetSymbolAddress (the set-up below) and passed to the kernels as their
+// workspace pointer.  An address belongs to a CUDA context, not to a device
+// ordinal: a host that drives its own driver-API context, or that reset the
+// device and so got a new primary context, needs a fresh lookup.  The cache
+// is therefore keyed by the current context's process-unique id
+// (cuCtxGetId), so the lookup runs once per context.
 #include <cstdio>
+#include <mutex>
 
 #include "kernels.cuh"
 
@@ -29,24 +33,44 @@ constexpr int64_t kMaxScratchFloats = 8ll << 20;
 
 static __device__ __align__(256) float g_fwd_scratch[kMaxScratchFloats];
 
-std::atomic<float*> g_scratch_addr[64];
+struct ScratchEntry {
+  unsigned long long ctx_id;
+  float* ptr;
+};
+constexpr int kCacheSlots = 64;
+ScratchEntry g_cache[kCacheSlots];  // guarded by g_cache_mu; ids are never reused in a process
+int g_cache_next = 0;
+std::mutex g_cache_mu;
 
-// Device address of g_fwd_scratch on the current device (looked up on the
-// first call per device, then cached).
+// Device address of g_fwd_scratch in the current context (looked up on the
+// first call in each context, then cached).
 int scratch_address(float** out) {
   int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess)
+  if (cudaGetDevice(&dev) != cudaSuccess)
     return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: cudaGetDevice failed");
-  if (dev < 0 || dev >= 64)
-    return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: device ordinal out of range");
-  float* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    err = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_fwd_scratch);
-    if (err != cudaSuccess || p == nullptr)
-      return cce::report_error(CCE_ERR_CUDA,
-                               "cce_forward_noalloc: cudaGetSymbolAddress of the static scratch failed");
-    g_scratch_addr[dev].store(p, std::memory_order_release);
+  unsigned long long id = 0;
+  if (!cce::current_context_id(&id))
+    return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: could not read the current CUDA context");
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  if (id != 0) {
+    for (int i = 0; i < kCacheSlots; ++i)
+      if (g_cache[i].ctx_id == id && g_cache[i].ptr != nullptr) {
+        *out = g_cache[i].ptr;
+        return CCE_OK;
+      }
+  }
+  // Miss: the runtime call below also makes the device's primary context
+  // current when no context was current yet.
+  float* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_fwd_scratch);
+  if (err != cudaSuccess || p == nullptr)
+    return cce::report_error(CCE_ERR_CUDA,
+                             "cce_forward_noalloc: cudaGetSymbolAddress of the static scratch failed");
+  if (id == 0 && !cce::current_context_id(&id))
+    return cce::report_error(CCE_ERR_CUDA, "cce_forward_noalloc: could not read the current CUDA context");
+  if (id != 0) {
+    g_cache[g_cache_next] = ScratchEntry{id, p};
+    g_cache_next = (g_cache_next + 1) % kCacheSlots;
   }
   *out = p;
   return CCE_OK;

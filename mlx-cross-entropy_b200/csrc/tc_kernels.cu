@@ -1211,19 +1211,31 @@ bool make_tmap_acc2(CUtensorMap* tm, const float* acc2, int64_t D, int64_t N) {
   return r == CUDA_SUCCESS;
 }
 
+// Opt a kernel into `bytes` of dynamic shared memory, once per CUDA context
+// (the attribute belongs to the context; `ctx_of` caches, per device ordinal,
+// the id of the context it was last set in).
+template <typename K>
+cudaError_t ensure_smem_attr(K kern, size_t bytes, std::atomic<unsigned long long> (&ctx_of)[64]) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  const bool slot = dev >= 0 && dev < 64;
+  unsigned long long ctx = 0;
+  if (slot && current_context_id(&ctx) && ctx != 0 && ctx_of[dev].load(std::memory_order_acquire) == ctx)
+    return cudaSuccess;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (err != cudaSuccess) return err;
+  if (slot && current_context_id(&ctx) && ctx != 0) ctx_of[dev].store(ctx, std::memory_order_release);
+  return cudaSuccess;
+}
+
 template <bool A_MN, bool B_MN, class Epi>
 cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
                         const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<A_MN, B_MN, Epi>;
-  static std::atomic<int> attr_done[64];
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  static std::atomic<unsigned long long> attr_ctx[64];
+  cudaError_t err = ensure_smem_attr(kern, SMEM_BYTES, attr_ctx);
   if (err != cudaSuccess) return err;
-  if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-    if (err != cudaSuccess) return err;
-    if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
-  }
   const int tiles = s.units();
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
@@ -1236,15 +1248,9 @@ template <bool A_MN, bool B_MN, class Epi>
 cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
                          const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm2_kernel<A_MN, B_MN, Epi>;
-  static std::atomic<int> attr_done[64];
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
+  static std::atomic<unsigned long long> attr_ctx[64];
+  cudaError_t err = ensure_smem_attr(kern, SMEM2_BYTES, attr_ctx);
   if (err != cudaSuccess) return err;
-  if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
-    if (err != cudaSuccess) return err;
-    if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_release);
-  }
   const int tiles = s.units();
   if (tiles == 0) return cudaSuccess;
   const int pairs = num_sms() / 2;

@@ -66,9 +66,12 @@ def cce_loss(e, c, targets, bias=None, reduction="mean", ignore_index=-100, *,
     return (loss, lse) if return_lse else loss
 
 
+IMPLS = ("auto", "fused", "chunked", "reference")
+
+
 def linear_cross_entropy(e, c, targets, bias=None, reduction="mean", ignore_index=-100,
-                         shift=0, return_lse=False, *, filter_log_eps=FILTER_LOG_EPS,
-                         skip_stats=None):
+                         shift=0, return_lse=False, impl="auto", compute_all_grads=False, *,
+                         filter_log_eps=FILTER_LOG_EPS, skip_stats=None):
     """Memory-efficient cross-entropy that never materialises [N, V] logits.
 
     Args (reference mlx_cce/__init__.py:79-107, reference/__init__.py:22-57):
@@ -81,12 +84,19 @@ def linear_cross_entropy(e, c, targets, bias=None, reduction="mean", ignore_inde
         shift: drop the last ``shift`` positions of e and the first ``shift``
             of targets along the sequence axis (causal-LM alignment)
         return_lse: also return the per-row log-sum-exp (float32, flat [N])
+        impl: accepted for signature compatibility with the research package
+            (reference/__init__.py:22-85, which picks one of several MLX / Metal
+            implementations); every value runs the one CUDA path here
+        compute_all_grads: accepted for signature compatibility; gradients
+            reach ``c`` and ``bias`` whenever those tensors require grad
     Returns:
         float32 loss scalar, or per-token loss shaped like ``targets`` for
         reduction="none"; ``(loss, lse)`` with ``return_lse``.
     """
     if reduction not in REDUCTIONS:
         raise ValueError(f"Unknown reduction: {reduction}")
+    if impl not in IMPLS:
+        raise ValueError(f"Unknown impl: {impl!r}; expected one of {IMPLS}")
     if shift:
         e = e[..., :-shift, :]
         targets = targets[..., shift:]
@@ -100,13 +110,20 @@ def linear_cross_entropy(e, c, targets, bias=None, reduction="mean", ignore_inde
 
 
 class LinearCrossEntropy(torch.nn.Module):
-    """Module form (reference/__init__.py:88-118)."""
+    """Module form (reference/__init__.py:88-118).
 
-    def __init__(self, reduction="mean", ignore_index=-100, shift=0):
+    ``criterion = LinearCrossEntropy(reduction="mean")`` then
+    ``loss = criterion(hidden_states, classifier_weight, targets, bias=None)``.
+    """
+
+    def __init__(self, reduction="mean", ignore_index=-100, shift=0, compute_all_grads=False):
         super().__init__()
+        if reduction not in REDUCTIONS:
+            raise ValueError(f"Unknown reduction: {reduction}")
         self.reduction = reduction
         self.ignore_index = ignore_index
         self.shift = shift
+        self.compute_all_grads = compute_all_grads
 
     def forward(self, e, c, targets, bias=None):
         return linear_cross_entropy(e, c, targets, bias=bias, reduction=self.reduction,

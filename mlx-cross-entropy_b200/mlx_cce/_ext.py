@@ -15,6 +15,7 @@ reference's C++ exceptions become Python exceptions through nanobind.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 import os
@@ -167,6 +168,20 @@ def _ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+def _alloc_on(stream):
+    """Context in which outputs and workspaces for a call on ``stream`` are allocated.
+
+    The caching allocator ties a block to the stream that allocated it: a
+    workspace freed when the call returns may be handed to the next
+    allocation on that same stream only.  Allocating on the launch stream
+    (not torch's current stream) keeps a kernel still running there from
+    sharing its memory with work on another stream.
+    """
+    if stream is None:
+        return contextlib.nullcontext()
+    return torch.cuda.stream(_torch_stream(stream))
+
+
 def _stream(stream=None):
     if stream is None:
         return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -228,11 +243,12 @@ def forward(e, c, targets, bias=None, v_offset: int = 0, stream=None):
     dt = dtype_code(e.dtype, what)
     bdt = dtype_code(bias.dtype, what) if bias is not None else 0
     nvt = num_stat_tiles(V)
-    tile_max = torch.empty((nvt, N), dtype=torch.float32, device=dev)
-    lse = torch.empty((N,), dtype=torch.float32, device=dev)
-    tgt = torch.empty((N,), dtype=torch.float32, device=dev)
     ws_bytes = int(lib.cce_forward_workspace_bytes(N, D, V, dt))
-    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    with _alloc_on(stream):
+        tile_max = torch.empty((nvt, N), dtype=torch.float32, device=dev)
+        lse = torch.empty((N,), dtype=torch.float32, device=dev)
+        tgt = torch.empty((N,), dtype=torch.float32, device=dev)
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
     with _Timed("forward", _torch_stream(stream) if _timing is not None else None):
         rc = lib.cce_forward(_ptr(e), _ptr(c), _ptr(bias), bdt, _ptr(targets), N, D, V, int(v_offset),
                              dt, _ptr(tile_max), _ptr(lse), _ptr(tgt), _ptr(ws), ws_bytes,
@@ -257,9 +273,10 @@ def lse_combine(part_lse, part_tgt=None, stream=None):
     if not part_lse.is_cuda:
         raise ValueError(f"[{what}] partials must be CUDA tensors")
     dev = part_lse.device
-    lse = torch.empty((N,), dtype=torch.float32, device=dev)
-    tgt = torch.empty((N,), dtype=torch.float32, device=dev) if part_tgt is not None else None
-    nll = torch.empty((N,), dtype=torch.float32, device=dev) if part_tgt is not None else None
+    with _alloc_on(stream):
+        lse = torch.empty((N,), dtype=torch.float32, device=dev)
+        tgt = torch.empty((N,), dtype=torch.float32, device=dev) if part_tgt is not None else None
+        nll = torch.empty((N,), dtype=torch.float32, device=dev) if part_tgt is not None else None
     rc = lib.cce_lse_combine(_ptr(part_lse), _ptr(part_tgt), P, N, part_lse.stride(0), _ptr(lse),
                              _ptr(tgt), _ptr(nll), _stream(stream))
     _check(rc, what)
@@ -289,18 +306,21 @@ def backward(e, c, targets, lse, d_nll, tile_max, bias=None, *, v_offset: int = 
         raise ValueError(f"[{what}] lse/d_nll must hold N={N} values and tile_max {num_stat_tiles(V)}x{N}")
     if need_bias and bias is None:
         raise ValueError(f"[{what}] need_bias without bias")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != V):
+        raise ValueError(f"[{what}] bias must be [V={V}], got {tuple(bias.shape)}")
     dt = dtype_code(e.dtype, what)
     bdt = dtype_code(bias.dtype, what) if bias is not None else 0
     flags = (CCE_NEED_DE if need_e else 0) | (CCE_NEED_DC if need_c else 0) | \
             (CCE_NEED_DBIAS if need_bias else 0) | (CCE_DE_F32 if grad_e_f32 else 0) | \
             (CCE_NO_FILTER if no_filter else 0)
-    grad_e = None
-    if need_e:
-        grad_e = torch.empty((N, D), dtype=torch.float32 if grad_e_f32 else e.dtype, device=dev)
-    grad_c = torch.empty((V, D), dtype=c.dtype, device=dev) if need_c else None
-    grad_b = torch.empty((V,), dtype=torch.float32, device=dev) if need_bias else None
     ws_bytes = int(lib.cce_backward_workspace_bytes(N, D, V, dt, flags))
-    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    with _alloc_on(stream):
+        grad_e = None
+        if need_e:
+            grad_e = torch.empty((N, D), dtype=torch.float32 if grad_e_f32 else e.dtype, device=dev)
+        grad_c = torch.empty((V, D), dtype=c.dtype, device=dev) if need_c else None
+        grad_b = torch.empty((V,), dtype=torch.float32, device=dev) if need_bias else None
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
     if skip_stats is not None and (skip_stats.dtype != torch.int64 or skip_stats.numel() < 2
                                    or not skip_stats.is_cuda):
         raise ValueError(f"[{what}] skip_stats must be a CUDA int64 tensor with 2 entries")
@@ -334,7 +354,8 @@ def dequantize(wq, scales, biases, group_size: int, bits: int, dtype, out=None, 
         raise ValueError(f"[{what}] scales must be [{rows}, {D // group_size}], got {tuple(scales.shape)}")
     dev = _require_cuda(what, wq=wq, scales=scales, biases=biases)
     if out is None:
-        out = torch.empty((rows, D), dtype=dtype, device=dev)
+        with _alloc_on(stream):
+            out = torch.empty((rows, D), dtype=dtype, device=dev)
     elif out.shape != (rows, D) or out.dtype != dtype or not out.is_contiguous():
         raise ValueError(f"[{what}] out must be a contiguous [{rows}, {D}] {dtype} tensor")
     rc = lib.cce_dequantize(_ptr(wq), _ptr(scales), _ptr(biases), dtype_code(scales.dtype, what), rows, D,

@@ -170,6 +170,76 @@ def test_batched_sequence():
     check(got, ref, torch.bfloat16)
 
 
+# --- API extras of the research package (reference/__init__.py:22-57, :88-118) ---
+
+@pytest.mark.parametrize("reduction", ["mean", "none"])
+def test_shift_drops_last_position_and_first_target(reduction):
+    """shift=1 (reference/_reference.py:15-17): e[..., :-1, :] is scored
+    against targets[..., 1:]; the dropped position gets no gradient."""
+    g = torch.Generator().manual_seed(51)
+    B, T, D, V = 3, 41, 128, 3000
+    e = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    c = (torch.randn(V, D, generator=g) * D ** -0.5).to(torch.bfloat16)
+    t = torch.randint(0, V, (B, T), generator=g)
+    t[:, 5] = -100
+    go = torch.randn(B, T - 1, generator=g) if reduction == "none" else None
+    got = run(e, c, t, reduction=reduction, grad_out=go, shift=1)
+    ref = oracle(e[:, :-1, :], c, t[:, 1:], reduction=reduction, grad_out=go)
+    if reduction == "none":
+        assert got["loss"].shape == (B, T - 1)
+    np.testing.assert_allclose(got["loss"].reshape(-1), np.asarray(ref["loss"]).reshape(-1),
+                               rtol=LOSS_RTOL[torch.bfloat16], atol=1e-6)
+    assert np.all(got["dE"][:, -1, :] == 0.0)
+    assert O.rel_max_abs(got["dE"][:, :-1, :].reshape(-1, D), ref["dE"]) < GRAD_TOL
+    assert O.rel_max_abs(got["dC"], ref["dC"]) < GRAD_TOL
+
+
+def test_return_lse_matches_oracle():
+    """return_lse=True (reference/_reference.py:30-31, :46-47) returns (loss,
+    lse) with lse the float32 log-sum-exp of every row (ignored rows too)."""
+    e, c, t, b = small(96, 64, 2000, torch.bfloat16, seed=52, bias=torch.float32, ignore=0.1)
+    dev = _dev()
+    ref = oracle(e, c, t, bias=b)
+    loss, lse = mlx_cce.linear_cross_entropy(e.to(dev), c.to(dev), t.to(dev), bias=b.to(dev),
+                                             return_lse=True)
+    assert lse.dtype == torch.float32 and lse.shape == (96,)
+    np.testing.assert_allclose(lse.double().cpu().numpy(), ref["lse"], rtol=1e-3)
+    np.testing.assert_allclose(loss.item(), ref["loss"], rtol=LOSS_RTOL[torch.bfloat16])
+    loss2, lse2 = mlx_cce.cce_loss(e.to(dev), c.to(dev), t.to(dev), bias=b.to(dev), return_lse=True)
+    np.testing.assert_allclose(lse2.cpu().numpy(), lse.cpu().numpy(), rtol=1e-6)
+    np.testing.assert_allclose(loss2.item(), loss.item(), rtol=1e-6)
+
+
+@pytest.mark.parametrize("reduction", ["sum", "none"])
+def test_linear_cross_entropy_module(reduction):
+    """LinearCrossEntropy (reference/__init__.py:88-118): a module holding
+    reduction / ignore_index / shift, called as criterion(e, c, targets, bias)."""
+    g = torch.Generator().manual_seed(53)
+    B, T, D, V = 2, 33, 64, 1500
+    e = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    c = (torch.randn(V, D, generator=g) * D ** -0.5).to(torch.bfloat16)
+    b = torch.randn(V, generator=g) * 0.3
+    t = torch.randint(0, V, (B, T), generator=g)
+    t[0, ::4] = 9
+    dev = _dev()
+    crit = mlx_cce.LinearCrossEntropy(reduction=reduction, ignore_index=9, shift=1,
+                                      compute_all_grads=True)
+    e_ = e.to(dev).requires_grad_(True)
+    c_ = c.to(dev).requires_grad_(True)
+    b_ = b.to(dev).requires_grad_(True)
+    loss = crit(e_, c_, t.to(dev), b_)
+    go = torch.linspace(-1.0, 1.0, B * (T - 1)).reshape(B, T - 1) if reduction == "none" else None
+    loss.backward(go.to(dev) if go is not None else None)
+    ref = oracle(e[:, :-1, :], c, t[:, 1:], bias=b, reduction=reduction, ignore_index=9,
+                 grad_out=go)
+    f = lambda x: x.detach().double().cpu().numpy()
+    np.testing.assert_allclose(f(loss).reshape(-1), np.asarray(ref["loss"]).reshape(-1),
+                               rtol=LOSS_RTOL[torch.bfloat16], atol=1e-6)
+    assert O.rel_max_abs(f(e_.grad)[:, :-1, :].reshape(-1, D), ref["dE"]) < GRAD_TOL
+    assert O.rel_max_abs(f(c_.grad), ref["dC"]) < GRAD_TOL
+    assert O.rel_max_abs(f(b_.grad), ref["dB"]) < GRAD_TOL
+
+
 def test_cut_cross_entropy_matches_cce_loss():
     e, c, t, _ = small(32, 64, 1024, torch.float32, seed=7)
     dev = _dev()
@@ -437,5 +507,11 @@ def test_workload5_full_size_sampled():
     dC_ref, _ = O.cols_grad_c(en, cn, safe, lse_gpu, d_nll, cols)
     dC_gpu = c_.grad[torch.as_tensor(cols, device=dev)].float().cpu().numpy()
     assert O.rel_max_abs(dC_gpu, dC_ref) < GRAD_TOL
+    # the loss: sum over valid rows of (lse - target logit), the target logits
+    # recomputed in float64 on the CPU and the GPU's lse checked above on the
+    # sampled rows
+    tgt64 = (e2.double() * c[torch.as_tensor(safe)].double()).sum(dim=1).numpy()
+    loss_ref = float(((lse_gpu - tgt64) * valid).sum())
+    np.testing.assert_allclose(loss.item(), loss_ref, rtol=1e-3)
     skipped, total = stats.tolist()
     assert total == (N // 128) * _ext.num_stat_tiles(V)
