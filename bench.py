@@ -173,7 +173,8 @@ def cpu_reference_step_fn(cfg, rows):
         cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
     except Exception:
         cores = os.cpu_count() or 1
-    sample = (f"first {rows} of {w.N} rows of config {cfg} against the full V={w.V} x D={w.D} "
+    what = f"all {rows} rows" if rows == w.N else f"first {rows} of {w.N} rows"
+    sample = (f"{what} of config {cfg} against the full V={w.V} x D={w.D} "
               f"classifier: chunked online-LSE forward + analytic dE/dC backward, float32 numpy")
     return step, sample, cores, w, rows
 
@@ -582,8 +583,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ref-rows", type=int, default=1024,
-                    help="rows of the workload in one step of the reference arm (--impl reference)")
+    ap.add_argument("--ref-rows", type=int, default=1 << 30,
+                    help="rows of the workload in one step of the reference arm (--impl reference; "
+                         "default: all of them)")
     ap.add_argument("--cpu-rows", type=int, default=256,
                     help="rows of the workload in the cpu_baseline leg of our arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
