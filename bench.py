@@ -567,10 +567,13 @@ def run_ours(args, rank, world, local_rank):
         if parity is not None:
             line["parity"] = parity
         print(json.dumps(line), flush=True)
-    # a graph holding NCCL calls must be released before the process group
+    # a graph holding NCCL calls must be released before the process group,
+    # and the exchange buffers (a collective) while it still exists
     del graph
     torch.cuda.synchronize()
     if world > 1:
+        from mlx_cce import _peer
+        _peer.release_all()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -217,6 +217,73 @@ CCE_API int cce_dequantize(const uint32_t* wq, const void* scales, const void* b
                            int64_t rows, int64_t D, int group_size, int bits, int out_dtype, void* out,
                            void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Vocabulary-sharded backward over NVLink peer memory.  No counterpart in the
+ * reference (it has no multi-device code); this is the cross-rank sum of
+ * grad_e that the sharded path needs, done with the ranks' own loads and
+ * stores instead of a collective library.
+ *
+ * Every rank of a group (one process per GPU of one node) allocates one
+ * exchange buffer with cce_peer_buffer_alloc, sends its IPC handle to every
+ * other rank (any host-side channel: the caller's process group), opens the
+ * others' handles with cce_peer_buffer_open, and passes all of them in a
+ * CcePeerGroup.  Buffers are allocated once per group, not per call (this is
+ * set-up, the only place this library allocates device memory).
+ * --------------------------------------------------------------------------- */
+
+#define CCE_PEER_MAX_WORLD    16
+#define CCE_PEER_HANDLE_BYTES 64   /* a cudaIpcMemHandle_t */
+/* cce_device_status codes of the exchange's bounded waits */
+#define CCE_PEER_WAIT_PUSH    201  /* a rank's partial grad_e never arrived      */
+#define CCE_PEER_WAIT_REDUCE  202  /* a rank's reduced rows never became ready   */
+
+typedef struct CcePeerGroup {
+  int32_t rank;            /* this rank, in [0, world)                              */
+  int32_t world;           /* ranks in the group, 1..CCE_PEER_MAX_WORLD              */
+  int64_t wait_limit_ns;   /* bound of each wait on another rank (<= 0: 10 s)        */
+  size_t bytes;            /* size of every rank's buffer (all equal)                */
+  void* bases[CCE_PEER_MAX_WORLD]; /* each rank's buffer as mapped in this process;
+                                      bases[rank] = this rank's own                  */
+} CcePeerGroup;
+
+/* Exchange-buffer size for N rows of grad_e [N, D] over `world` ranks, the
+ * result written in out_dtype (CCE_F32 / F16 / BF16). */
+CCE_API size_t cce_peer_buffer_bytes(int64_t N, int64_t D, int world, int out_dtype);
+
+/* Allocates a zero-initialised exchange buffer on the current device and
+ * writes its IPC handle (CCE_PEER_HANDLE_BYTES bytes) to ipc_handle. */
+CCE_API int cce_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Maps another rank's buffer into this process (enables peer access). */
+CCE_API int cce_peer_buffer_open(const void* ipc_handle, void** ptr);
+/* Unmaps a buffer opened with cce_peer_buffer_open. */
+CCE_API int cce_peer_buffer_close(void* ptr);
+/* Frees a buffer from cce_peer_buffer_alloc (after every rank closed it). */
+CCE_API int cce_peer_buffer_free(void* ptr);
+
+/*
+ * cce_backward_peer -- cce_backward for one vocabulary shard, with grad_e
+ * summed over the group: on return (in stream order) every rank's grad_e holds
+ * the full sum of all ranks' partials, in e's dtype (fp32 with CCE_DE_F32).
+ * Arguments as cce_backward (c, bias, V, v_offset are this rank's shard; lse
+ * the global one); grad_c / grad_bias stay sharded.  Every rank of the group
+ * must make the same sequence of calls with the same N, D, dtype and flags.
+ *
+ * The last vocabulary chunk's grad_e GEMM stores each output tile straight
+ * into the owning rank's buffer over NVLink (rows are owned in 128-row tiles),
+ * each owner sums its rows in rank order (deterministic), and every rank
+ * copies the other ranks' summed rows.  Waits on other ranks are bounded by
+ * group->wait_limit_ns; when one runs out the call's grad_e is invalid,
+ * cce_device_status reports CCE_PEER_WAIT_PUSH / _REDUCE, and the group's
+ * buffers must be re-created.
+ */
+CCE_API int cce_backward_peer(const void* e, const void* c, const void* bias, int bias_dtype,
+                              const int32_t* targets, const float* lse, const float* d_nll,
+                              const float* tile_max, int64_t N, int64_t D, int64_t V,
+                              int64_t v_offset, int dtype, int flags, float filter_log_eps,
+                              void* grad_e, void* grad_c, float* grad_bias, int64_t* skip_stats,
+                              void* workspace, size_t workspace_bytes, const CcePeerGroup* group,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "kernels.cuh"
@@ -240,9 +241,12 @@ uint64_t cce_launch_count(void) { return cce::g_launches.load(std::memory_order_
 
 int cce_device_status(int reset) {
   const int v = cce::tc_read_status(reset != 0);
-  if (v < 0) return fail(CCE_ERR_CUDA, "cce_device_status: could not read the device status word");
+  const int pv = cce::peer::read_status(reset != 0);
+  if (v < 0 || pv < 0) return fail(CCE_ERR_CUDA, "cce_device_status: could not read the device status words");
   if (v > 0)
     return fail(CCE_ERR_CUDA, "a tensor-core kernel abandoned a pipeline wait after its time limit (code %d)", v);
+  if (pv > 0)
+    return fail(CCE_ERR_CUDA, "a grad_e exchange kernel gave up waiting for another rank (code %d)", pv);
   return CCE_OK;
 }
 
@@ -327,12 +331,14 @@ size_t cce_backward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, 
   return b;
 }
 
-int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
-                 const int32_t* targets, const float* lse, const float* d_nll,
-                 const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
-                 int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
-                 float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
-                 void* stream) {
+// cce_backward, and cce_backward_peer when `pg` is given (grad_e summed over
+// the group through the exchange buffers).
+static int backward_impl(const void* e, const void* c, const void* bias, int bias_dtype,
+                         const int32_t* targets, const float* lse, const float* d_nll,
+                         const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                         int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
+                         float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
+                         const CcePeerGroup* pg, void* stream) {
   int rc = check_sizes(N, D, V, dtype);
   if (rc) return rc;
   if (bias && !dtype_ok(bias_dtype)) return fail(CCE_ERR_DTYPE, "unsupported bias dtype code %d", bias_dtype);
@@ -363,6 +369,22 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
   const size_t need = cce_backward_workspace_bytes(N, D, V, dtype, flags);
   if (!workspace || workspace_bytes < need)
     return fail(CCE_ERR_WORKSPACE, "cce_backward: workspace %zu bytes < required %zu", workspace_bytes, need);
+
+  // the cross-rank exchange of grad_e (only when grad_e is requested)
+  const bool exchange = pg != nullptr && need_de;
+  cce::PeerPush push{};
+  uint64_t wait_ns = 0;
+  const int out_dtype = (flags & CCE_DE_F32) ? CCE_F32 : dtype;
+  if (exchange) {
+    push.layout = cce::peer::make_layout(N, D, pg->world, (int)dtype_size(out_dtype));
+    if (pg->bytes < push.layout.bytes)
+      return fail(CCE_ERR_WORKSPACE, "cce_backward_peer: exchange buffers of %zu bytes < required %zu", pg->bytes,
+                  push.layout.bytes);
+    push.peers.rank = pg->rank;
+    push.peers.world = pg->world;
+    for (int r = 0; r < pg->world; ++r) push.peers.bases[r] = static_cast<char*>(pg->bases[r]);
+    wait_ns = pg->wait_limit_ns > 0 ? (uint64_t)pg->wait_limit_ns : 10000000000ull;
+  }
 
   char* ws = (char*)workspace;
   uint8_t* keep = (uint8_t*)ws;
@@ -413,10 +435,14 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
       CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->ev_l, 0), "cce_backward wait");
       CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->ev_l, 0), "cce_backward wait");
       if (need_de) {
-        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, ss->se), "cce_backward tc grad_e");
-        if (last)
-          CCE_CUDA_CHECK(cce::launch_sum2_f32(acc, acc + N * D, grad_e, (flags & CCE_DE_F32) ? CCE_F32 : dtype,
-                                              N * D, ss->se),
+        const bool push_now = exchange && last;
+        CCE_CUDA_CHECK(cce::tc_grad_e(a, acc, ch > 0, push_now ? &push : nullptr, ss->se), "cce_backward tc grad_e");
+        if (push_now)
+          CCE_CUDA_CHECK(cce::peer::launch_reduce_gather(push.peers, push.layout, cce::peer::kSlotsPerSrc, N, D,
+                                                         out_dtype, grad_e, wait_ns, ss->se),
+                         "cce_backward_peer exchange");
+        else if (last)
+          CCE_CUDA_CHECK(cce::launch_sum2_f32(acc, acc + N * D, grad_e, out_dtype, N * D, ss->se),
                          "cce_backward sum grad_e");
       }
       if (need_dc) CCE_CUDA_CHECK(cce::tc_grad_c(a, grad_c, ss->sc), "cce_backward tc grad_c");
@@ -430,10 +456,86 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
       CCE_CUDA_CHECK(cce::simt_dlogits(a, s), "cce_backward simt dlogits");
       if (need_de) CCE_CUDA_CHECK(cce::simt_grad_e(a, acc, ch > 0, s), "cce_backward simt grad_e");
       if (need_dc) CCE_CUDA_CHECK(cce::simt_grad_c(a, grad_c, s), "cce_backward simt grad_c");
-      if (need_de && last && !(flags & CCE_DE_F32))
+      if (need_de && last && exchange) {
+        CCE_CUDA_CHECK(cce::peer::launch_push(push.peers, push.layout, acc, 1, N, D, s), "cce_backward_peer push");
+        CCE_CUDA_CHECK(cce::peer::launch_reduce_gather(push.peers, push.layout, 1, N, D, out_dtype, grad_e, wait_ns, s),
+                       "cce_backward_peer exchange");
+      } else if (need_de && last && !(flags & CCE_DE_F32)) {
         CCE_CUDA_CHECK(cce::launch_cast_f32(acc, grad_e, dtype, N * D, s), "cce_backward cast grad_e");
+      }
     }
   }
+  return CCE_OK;
+}
+
+int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
+                 const int32_t* targets, const float* lse, const float* d_nll,
+                 const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                 int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
+                 float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  return backward_impl(e, c, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype, flags,
+                       filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes, nullptr,
+                       stream);
+}
+
+int cce_backward_peer(const void* e, const void* c, const void* bias, int bias_dtype,
+                      const int32_t* targets, const float* lse, const float* d_nll,
+                      const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                      int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
+                      float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
+                      const CcePeerGroup* group, void* stream) {
+  if (!group) return fail(CCE_ERR_ARG, "cce_backward_peer: NULL group");
+  if (group->world < 1 || group->world > CCE_PEER_MAX_WORLD || group->rank < 0 || group->rank >= group->world)
+    return fail(CCE_ERR_ARG, "cce_backward_peer: rank %d / world %d out of range (world <= %d)", group->rank,
+                group->world, CCE_PEER_MAX_WORLD);
+  for (int r = 0; r < group->world; ++r)
+    if (!group->bases[r] || !aligned16(group->bases[r]))
+      return fail(CCE_ERR_ARG, "cce_backward_peer: buffer of rank %d is NULL or not 16-byte aligned", r);
+  return backward_impl(e, c, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype, flags,
+                       filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes, group,
+                       stream);
+}
+
+size_t cce_peer_buffer_bytes(int64_t N, int64_t D, int world, int out_dtype) {
+  if (N < 0 || D <= 0 || world < 1 || world > CCE_PEER_MAX_WORLD || !dtype_ok(out_dtype)) return 0;
+  return cce::peer::make_layout(N, D, world, (int)dtype_size(out_dtype)).bytes;
+}
+
+int cce_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle) return fail(CCE_ERR_ARG, "cce_peer_buffer_alloc: NULL output pointer");
+  if (bytes < cce::peer::kCtrlBytes) return fail(CCE_ERR_ARG, "cce_peer_buffer_alloc: %zu bytes is too small", bytes);
+  int rc = check_arch();
+  if (rc) return rc;
+  void* p = nullptr;
+  CCE_CUDA_CHECK(cudaMalloc(&p, bytes), "cce_peer_buffer_alloc cudaMalloc");
+  cudaError_t err = cudaMemset(p, 0, bytes);
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(err, "cce_peer_buffer_alloc");
+  }
+  *ptr = p;
+  return CCE_OK;
+}
+
+int cce_peer_buffer_open(const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return fail(CCE_ERR_ARG, "cce_peer_buffer_open: NULL pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  CCE_CUDA_CHECK(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cce_peer_buffer_open");
+  return CCE_OK;
+}
+
+int cce_peer_buffer_close(void* ptr) {
+  if (!ptr) return CCE_OK;
+  CCE_CUDA_CHECK(cudaIpcCloseMemHandle(ptr), "cce_peer_buffer_close");
+  return CCE_OK;
+}
+
+int cce_peer_buffer_free(void* ptr) {
+  if (!ptr) return CCE_OK;
+  CCE_CUDA_CHECK(cudaFree(ptr), "cce_peer_buffer_free");
   return CCE_OK;
 }
 

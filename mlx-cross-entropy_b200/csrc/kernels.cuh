@@ -4,6 +4,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace cce {
 
@@ -99,10 +100,30 @@ cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
 cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
 // acc2[2][N][D] fp32: each output tile's two K halves of this chunk are
 // stored (accumulate = false) or added into slabs 0 and 1; grad_e is
-// acc2[0] + acc2[1] after the last chunk (launch_sum2_f32).
-cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t stream);
+// acc2[0] + acc2[1] after the last chunk (launch_sum2_f32).  With `push`
+// (the last chunk of a vocabulary-sharded backward) each half, plus its slab
+// when accumulating, goes to its rows' owner rank instead (peer.cuh).
+struct PeerPush {
+  peer::Peers peers;
+  peer::Layout layout;
+};
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, const PeerPush* push,
+                      cudaStream_t stream);
 cudaError_t tc_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
 // one bounded pipeline wait that nothing satisfies: records `code` after limit_ns
 cudaError_t tc_selftest_wait(uint64_t limit_ns, int code, cudaStream_t stream);
+
+// ---- cross-rank grad_e exchange (peer.cu) ----
+namespace peer {
+// partial rows src[nslab][N][D] fp32 -> their owners' receive slots; raises `pushed`
+cudaError_t launch_push(const Peers& P, const Layout& L, const float* src, int nslab, int64_t N, int64_t D,
+                        cudaStream_t stream);
+// reduce this rank's rows (nslot slots per source) into out (out_dtype) and the
+// reduced area, then gather the other ranks' rows into out
+cudaError_t launch_reduce_gather(const Peers& P, const Layout& L, int nslot, int64_t N, int64_t D, int out_dtype,
+                                 void* out, uint64_t limit_ns, cudaStream_t stream);
+// status word of the exchange kernels' bounded waits (0 = ok, -1 = read failed)
+int read_status(bool reset);
+}  // namespace peer
 
 }  // namespace cce

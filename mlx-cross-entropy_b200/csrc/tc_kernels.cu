@@ -71,6 +71,7 @@ static_assert(BN == kTcLseTile, "one LSE partial per output tile");
 constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-mask slice (bits)
 constexpr uint32_t OUT_STAGE_BYTES = 4 * 4096;  // epilogue output staging, 4 KB per epilogue warp
 constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
+constexpr int kPushWaitCode = 8;  // status code: a push unit's epilogue threads never all arrived
 
 // ---------------------------------------------------------------------------
 // helpers for the epilogues
@@ -253,6 +254,7 @@ struct FwdEpi {
       part_s[idx] = st.s;
     }
   }
+  __device__ __forceinline__ void after_unit(uint64_t*, uint32_t&) const {}
 };
 
 // ---------------------------------------------------------------------------
@@ -272,10 +274,6 @@ struct DlogitsEpi {
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
   int64_t N, V, v_offset, vc0, vc_end, ld;
-  // 1: every column group of an active tile is written (the CTA-pair grad
-  // GEMMs read whole 256-row tiles); 0: only 128-column halves holding a kept
-  // group (the single-CTA grad_c reads 128-row tiles, grad_e kept groups).
-  int all_groups;
 
   struct State {
     int64_t row, tl, col0;
@@ -297,7 +295,7 @@ struct DlogitsEpi {
   // Column groups the MMA computes: only the kept ones (the epilogue never
   // reads the accumulator columns of the others).
   __device__ __forceinline__ uint32_t col_mask(const MaskView& mk, int mb, int nb) const {
-    return all_groups ? kAllGroups : group_mask(mk, mb, nb);
+    return group_mask(mk, mb, nb);
   }
   __device__ __forceinline__ bool chunk_live(const State& st, int c) const {
     return (st.kmask >> (c / kChunksPerStat)) & 1u;
@@ -344,7 +342,7 @@ struct DlogitsEpi {
     // grad_c multiplies whole 128-column quarters (its M tiles): a quarter
     // with a kept group is stored whole (zeros in the others), the rest never
     // read; grad_e reads kept groups only.
-    if (all_groups || ((st.kmask >> (kStatsPerM * (c >> 2))) & ((1u << kStatsPerM) - 1u)))
+    if ((st.kmask >> (kStatsPerM * (c >> 2))) & ((1u << kStatsPerM) - 1u))
       sg.store16<T>(v, (int)(cb - vc0), st.y0);
     if (grad_bias != nullptr) {
       const int lane = threadIdx.x & 31;
@@ -354,6 +352,7 @@ struct DlogitsEpi {
   }
 
   __device__ __forceinline__ void end(State&) const {}
+  __device__ __forceinline__ void after_unit(uint64_t*, uint32_t&) const {}
 };
 
 // ---------------------------------------------------------------------------
@@ -365,6 +364,12 @@ struct DlogitsEpi {
 // store in the first chunk, a TMA reduce-add after it), so every slab has one
 // writer per chunk and the sums are deterministic.  The caller adds the two
 // slabs into grad_e after the last chunk.
+//
+// Push mode (the last chunk of a vocabulary-sharded backward): a unit's result
+// plus its slab's earlier chunks is stored straight into the receive slot
+// (this rank, split) of the rank that owns its rows (peer.cuh), with plain
+// 16-byte stores over NVLink while the MMAs of the next units run; the last
+// unit raises the `pushed` flag on every rank.  The slabs are not written.
 struct GradEEpi {
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
@@ -373,6 +378,10 @@ struct GradEEpi {
   int accumulate;
   float* acc2;              // [2][N][D]: zero tiles of the first chunk are stored directly
   int64_t N, D;
+  int push;                 // push mode (then the fields below are set)
+  unsigned total_units;     // work units of the launch
+  peer::Peers peers;
+  peer::Layout layout;
 
   struct State {
     int64_t col0;
@@ -426,12 +435,62 @@ struct GradEEpi {
     st.y0 = mb * BM + r - (int)(threadIdx.x & 31);
     st.ks = ks;
   }
+  // Push mode has no zero-tile shortcut: an empty unit still sends its slab.
+  __device__ __forceinline__ bool zero_shortcut() const { return push == 0; }
   __device__ __forceinline__ void chunk(State& st, int c, float (&v)[32], Stager& sg) const {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= st.s;
+    if (push) {
+      push_chunk(st, c, v, sg);
+      return;
+    }
     sg.store_f32(v, (int)(st.col0 + c * 32), st.y0, st.ks, accumulate != 0);
   }
+  // The warp's 32 rows x 32 columns go through its 4 KB staging area (16-byte
+  // units of row r at unit u ^ (r & 7): conflict-free both ways), then leave
+  // as 4 rows x 128 contiguous bytes per store instruction.
+  __device__ __forceinline__ void push_chunk(const State& st, int c, const float (&v)[32], Stager& sg) const {
+    const int lane = threadIdx.x & 31;
+    float4* buf = reinterpret_cast<float4*>(sg.buf);
+    __syncwarp();  // the previous chunk's reads of the staging area are done
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      buf[lane * 8 + (u ^ (lane & 7))] = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+    __syncwarp();
+    const int u = lane & 7;
+    const int64_t col = st.col0 + c * 32 + 4 * u;
+    const int owner = (int)((st.y0 / peer::kRows) / layout.mt_per);
+    float* slot = reinterpret_cast<float*>(peers.bases[owner] + layout.recv_off) +
+                  ((int64_t)(peers.rank * peer::kSlotsPerSrc + st.ks) * layout.R - (int64_t)owner * layout.R) * D;
+    const float* slab = acc2 + (int64_t)st.ks * N * D;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = 4 * i + (lane >> 3);
+      const int64_t row = (int64_t)st.y0 + rr;
+      float4 x = buf[rr * 8 + (u ^ (rr & 7))];
+      if (row < N && col < D) {
+        if (accumulate) {
+          const float4 a = *reinterpret_cast<const float4*>(slab + row * D + col);
+          x.x += a.x;
+          x.y += a.y;
+          x.z += a.z;
+          x.w += a.w;
+        }
+        *reinterpret_cast<float4*>(slot + row * D + col) = x;
+      }
+    }
+  }
   __device__ __forceinline__ void end(State&) const {}
+  // Push mode: once all 128 epilogue threads' stores of the unit are issued
+  // (they arrive on `ubar`; the wait is bounded), one thread publishes them
+  // and counts the unit; the last unit of the launch raises `pushed`.
+  __device__ __forceinline__ void after_unit(uint64_t* ubar, uint32_t& uphase) const {
+    if (!push) return;
+    mbar_arrive(ubar);
+    if (threadIdx.x == 64 && mbar_wait(ubar, uphase, kPushWaitCode))
+      peer::arrive_and_signal(peers, peer::kDoneUnitsOff, total_units, true, peer::kPushedOff);
+    uphase ^= 1u;
+  }
 };
 
 // ---------------------------------------------------------------------------
@@ -471,6 +530,7 @@ struct GradCEpi {
     return max(kb, r * kKpr);
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
+  __device__ __forceinline__ bool zero_shortcut() const { return true; }
   // A tile no K-block reached is zero: lane l stores 8 columns of each row.
   __device__ __forceinline__ void zero_tile(const State& st) const {
     const int64_t c0 = st.col0 + 8 * (threadIdx.x & 31);
@@ -492,6 +552,7 @@ struct GradCEpi {
     sg.store16<T>(v, (int)(st.col0 + c * 32), st.y0);
   }
   __device__ __forceinline__ void end(State&) const {}
+  __device__ __forceinline__ void after_unit(uint64_t*, uint32_t&) const {}
 };
 
 // ---------------------------------------------------------------------------
@@ -567,6 +628,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* rempty = rfull + RING;   // released by the MMA thread + 128 epilogue threads
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RING);
   volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* ubar = full + 23;        // epilogue unit barrier (bytes 184-191; the ring ends at 180)
   uint8_t* smask = reinterpret_cast<uint8_t*>(full) + 256;
 
   const int warp = threadIdx.x >> 5;
@@ -586,6 +648,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(rfull + i, 1);
       mbar_init(rempty + i, 129);
     }
+    mbar_init(ubar, 128);
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -741,6 +804,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     Stager sg{&tmC, sOut + q * 4096, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t uphase = 0;
     for (int i = 0;; ++i) {
       const int slot = i & (RING - 1);
       if (!mbar_wait(rfull + slot, (i / RING) & 1, 7)) break;
@@ -763,7 +827,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // a tile no K-block reached is all zeros: plain coalesced zero stores
       // (or nothing, when zeros would be added), not the staged path
       bool zero_tile = false;
-      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb;
+      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb && epi.zero_shortcut();
       if (zero_tile) {
         if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
       } else {
@@ -781,6 +845,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       epi.end(st);
+      epi.after_unit(ubar, uphase);
       __syncwarp();
       tc_fence_before();
       mbar_arrive(tempty + acc);
@@ -798,300 +863,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
-
-// ---------------------------------------------------------------------------
-// the CTA-pair engine (cta_group::2)
-//
-// Clusters of two CTAs on two SMs compute 256 x 256 tiles: CTA r holds rows
-// [128 r, 128 r + 128) of the A slice and columns [128 r, 128 r + 128) of the
-// B slice (32 KB per stage, 6 stages) and accumulates its 128 rows x 256
-// columns in its own TMEM.  The leader (rank 0) issues every
-// tcgen05.mma.cta_group::2; both CTAs' TMA loads complete on the leader's
-// `full` barrier; the leader's commits arrive on each CTA's own `empty` and
-// `tfull` barriers; both epilogues release the accumulator on the leader's
-// `tempty`.  Tile ids come from the leader's producer, which writes them into
-// both CTAs' rings (distributed shared memory).  Per SM this halves the B
-// traffic of the 1-CTA engine for the same FLOPs.
-// ---------------------------------------------------------------------------
-
-constexpr int STAGES2 = 6;
-constexpr uint32_t A2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 rows of A
-constexpr uint32_t B2_BYTES = 128 * BK * 2;   // 16 KB: this CTA's 128 columns of B
-constexpr uint32_t STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr size_t SMEM2_BYTES = 1024 + STAGES2 * (size_t)STAGE2_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
-
-template <bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
-tc_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, const Sched sched, const Epi epi,
-                const uint32_t idesc) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
-  uint8_t* smem = smem_raw + pad;
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES2 * A2_BYTES;
-  uint8_t* sOut = sB + STAGES2 * B2_BYTES;   // epilogue staging (1 KB aligned)
-  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + OUT_STAGE_BYTES);
-  uint64_t* empty = full + STAGES2;
-  uint64_t* tfull = empty + STAGES2;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* rfull = tempty + 2;
-  uint64_t* rempty = rfull + RING;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RING);
-  volatile int* ring = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint8_t* smask = reinterpret_cast<uint8_t*>(full) + 256;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const bool leader = rank == 0;
-  const uint32_t peer = rank ^ 1u;
-  const int num_tiles = sched.units();
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES2; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, 256);   // both CTAs' epilogue threads
-    }
-    for (int i = 0; i < RING; ++i) {
-      mbar_init(rfull + i, 1);
-      mbar_init(rempty + i, 258);   // leader MMA + 2 x 128 epilogue + peer producer
-    }
-    fence_barrier_init();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-  }
-  MaskView mk{nullptr, nullptr, 0, 0, 0};
-  load_mask_view<Epi>(epi, smask, mk);
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, TMEM_COLS);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();   // the peer's barriers are initialised before any remote access
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  // A pair tile is active / has an active K-block when either CTA's half does.
-  auto tile_on = [&](int mb, int nb) {
-    return epi.tile_active(mk, 2 * mb, nb) || epi.tile_active(mk, 2 * mb + 1, nb);
-  };
-  auto next_on = [&](int mb, int nb, int kb, int kb1) {
-    return min(epi.next_kb(mk, 2 * mb, nb, kb, kb1), epi.next_kb(mk, 2 * mb + 1, nb, kb, kb1));
-  };
-  const uint32_t full_leader = mapa_shared(smem_u32(full), 0);   // + 8 * stage
-  const uint32_t rempty_leader = mapa_shared(smem_u32(rempty), 0);
-  const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
-
-  if (warp == 0) {
-    // ---------------- TMA producers (both CTAs); tile scheduler (leader) ----------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int next = leader ? (sched.counter ? atomicAdd(sched.counter, 1) : (int)(blockIdx.x >> 1)) : 0;
-      const uint32_t ring_peer = mapa_shared(smem_u32((const void*)ring), peer);
-      const uint32_t rfull_peer = mapa_shared(smem_u32(rfull), peer);
-      for (int i = 0;; ++i) {
-        const int slot = i & (RING - 1);
-        const uint32_t rpar = (i / RING) & 1;
-        int tile;
-        if (leader) {
-          if (!mbar_wait(rempty + slot, rpar ^ 1u, 5)) break;
-          tile = next < num_tiles ? next : -1;
-          ring[slot] = tile;
-          st_cluster_u32(ring_peer + 4 * slot, (uint32_t)tile);
-          mbar_arrive(rfull + slot);
-          mbar_arrive_cluster(rfull_peer + 8 * slot);
-          if (tile >= 0)
-            next = sched.counter ? atomicAdd(sched.counter, 1)
-                                 : (int)(blockIdx.x >> 1) + (i + 1) * (int)(gridDim.x >> 1);
-        } else {
-          if (!mbar_wait_cluster(rfull + slot, rpar, 5)) break;
-          tile = ring[slot];
-          mbar_arrive_cluster(rempty_leader + 8 * slot);
-        }
-        if (tile < 0) break;
-        int mb, nb, ks, kb0, kb1;
-        sched.coords(tile, mb, nb, ks);
-        sched.krange(ks, kb0, kb1);
-        if (!tile_on(mb, nb)) continue;
-        bool ok = true;
-        const int arow = mb * 256 + (int)rank * 128;   // this CTA's A rows (or MN columns)
-        const int bcol = nb * 256 + (int)rank * 128;   // this CTA's B columns
-        for (int kb = next_on(mb, nb, kb0, kb1); kb < kb1; kb = next_on(mb, nb, kb + 1, kb1)) {
-          if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
-          if (leader) mbar_arrive_expect_tx(full + stage, 2 * STAGE2_BYTES);
-          const uint32_t fb = full_leader + 8 * stage;
-          uint8_t* a = sA + stage * A2_BYTES;
-          uint8_t* b = sB + stage * B2_BYTES;
-          const int k0 = kb * BK;
-          if (A_MN) {
-            if (sched.a3d) {
-              tma_load_3d_pair(a, &tmA, fb, 0, k0, arow / 64);
-            } else {
-              tma_load_2d_pair(a, &tmA, fb, arow, k0);
-              tma_load_2d_pair(a + BOX_MN_BYTES, &tmA, fb, arow + 64, k0);
-            }
-          } else {
-            tma_load_2d_pair(a, &tmA, fb, k0, arow);
-          }
-          if (B_MN) {
-            if (sched.b3d) {
-              tma_load_3d_pair(b, &tmB, fb, 0, k0, bcol / 64);
-            } else {
-              tma_load_2d_pair(b, &tmB, fb, bcol, k0);
-              tma_load_2d_pair(b + BOX_MN_BYTES, &tmB, fb, bcol + 64, k0);
-            }
-          } else {
-            tma_load_2d_pair(b, &tmB, fb, k0, bcol);
-          }
-          if (++stage == STAGES2) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (leader only) ----------------
-    if (lane == 0 && leader) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      const uint64_t adesc0 = A_MN ? smem_desc(smem_u32(sA), BOX_MN_BYTES, 1024)
-                                   : smem_desc(smem_u32(sA), 16, 1024);
-      const uint64_t bdesc0 = B_MN ? smem_desc(smem_u32(sB), BOX_MN_BYTES, 1024)
-                                   : smem_desc(smem_u32(sB), 16, 1024);
-      constexpr uint32_t a_kstep = (A_MN ? 2048u : 32u) >> 4;
-      constexpr uint32_t b_kstep = (B_MN ? 2048u : 32u) >> 4;
-      const uint32_t empty_peer = mapa_shared(smem_u32(empty), peer);
-      const uint32_t empty_self = mapa_shared(smem_u32(empty), rank);
-      const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), peer);
-      const uint32_t tfull_self = mapa_shared(smem_u32(tfull), rank);
-      for (int i = 0;; ++i) {
-        const int slot = i & (RING - 1);
-        if (!mbar_wait(rfull + slot, (i / RING) & 1, 6)) break;
-        const int tile = ring[slot];
-        mbar_arrive(rempty + slot);
-        if (tile < 0) break;
-        int mb, nb, ks, kb0, kb1;
-        sched.coords(tile, mb, nb, ks);
-        sched.krange(ks, kb0, kb1);
-        if (!tile_on(mb, nb)) continue;
-        if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        bool ok = true;
-        uint32_t issued = 0;
-        for (int kb = next_on(mb, nb, kb0, kb1); kb < kb1; kb = next_on(mb, nb, kb + 1, kb1)) {
-          if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t ad = adesc0 + (uint64_t)((stage * A2_BYTES) >> 4);
-          const uint64_t bd = bdesc0 + (uint64_t)((stage * B2_BYTES) >> 4);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_f16_pair(d_tmem, ad + k * a_kstep, bd + k * b_kstep, idesc,
-                         (issued | (uint32_t)k) != 0 ? 1u : 0u);
-          ++issued;
-          mma_commit_pair(empty_self + 8 * stage);
-          mma_commit_pair(empty_peer + 8 * stage);
-          if (++stage == STAGES2) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        mma_commit_pair(tfull_self + 8 * acc);
-        mma_commit_pair(tfull_peer + 8 * acc);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
-      }
-    }
-    __syncwarp();
-  } else {
-    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    Stager sg{&tmC, sOut + q * 4096, 0};
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int i = 0;; ++i) {
-      const int slot = i & (RING - 1);
-      const uint32_t rpar = (i / RING) & 1;
-      int tile;
-      if (leader) {
-        if (!mbar_wait(rfull + slot, rpar, 7)) break;
-        tile = ring[slot];
-        mbar_arrive(rempty + slot);
-      } else {
-        if (!mbar_wait_cluster(rfull + slot, rpar, 7)) break;
-        tile = ring[slot];
-        mbar_arrive_cluster(rempty_leader + 8 * slot);
-      }
-      if (tile < 0) break;
-      int mb, nb, ks, kb0, kb1;
-      sched.coords(tile, mb, nb, ks);
-      sched.krange(ks, kb0, kb1);
-      const int vmb = 2 * mb + (int)rank;   // this CTA's 128-row block
-      if (!tile_on(mb, nb)) {
-        epi.inactive_tile(vmb, nb, r);
-        continue;
-      }
-      if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
-      tc_fence_after();
-      const bool any_kb = !Epi::kMask || next_on(mb, nb, kb0, kb1) < kb1;
-      typename Epi::State st;
-      epi.begin(st, mk, vmb, nb, r, ks);
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      // a tile no K-block reached is all zeros: plain coalesced zero stores
-      // (or nothing, when zeros would be added), not the staged path
-      bool zero_tile = false;
-      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb;
-      if (zero_tile) {
-        if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          __syncwarp();
-          if (any_kb && epi.chunk_live(st, c)) {
-            tmem_ld32(tbase + c * 32, v);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-          }
-          epi.chunk(st, c, v, sg);
-        }
-      }
-      epi.end(st);
-      __syncwarp();
-      tc_fence_before();
-      if (leader) {
-        mbar_arrive(tempty + acc);
-      } else {
-        mbar_arrive_cluster(tempty_leader + 8 * acc);
-      }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
-    }
-    sg.drain();  // output boxes written before the kernel ends
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();   // neither CTA leaves while the other may still touch its shared memory
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem_base, TMEM_COLS);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // host side
@@ -1244,47 +1015,6 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   return launched();
 }
 
-template <bool A_MN, bool B_MN, class Epi>
-cudaError_t launch_gemm2(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
-                         const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
-  auto kern = tc_gemm2_kernel<A_MN, B_MN, Epi>;
-  static std::atomic<unsigned long long> attr_ctx[64];
-  cudaError_t err = ensure_smem_attr(kern, SMEM2_BYTES, attr_ctx);
-  if (err != cudaSuccess) return err;
-  const int tiles = s.units();
-  if (tiles == 0) return cudaSuccess;
-  const int pairs = num_sms() / 2;
-  const int grid = 2 * (tiles < pairs ? tiles : pairs);
-  const uint32_t idesc = instr_desc(256, BN, bf16, A_MN, B_MN);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = SMEM2_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, s, epi, idesc);
-  if (err != cudaSuccess) return err;
-  return launched();
-}
-
-// CCE_TC_PAIR=1 selects the CTA-pair engine.  It passes the same tests but
-// measured no faster than the single-CTA engine on B200 (both run into the
-// 1 kW power cap, at ~1.5 GHz, with the tensor pipe ~86% busy), so the
-// single-CTA engine is the default.
-bool use_pair() {
-  static const bool v = [] {
-    const char* e = getenv("CCE_TC_PAIR");
-    return e != nullptr && e[0] == '1';
-  }();
-  return v;
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -1307,14 +1037,12 @@ template <typename TB>
 cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
   CUtensorMap tmA, tmB;
-  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, pair ? BN / 2 : BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
+  if (!make_tmap(&tmB, a.c, bf16, a.D, a.V, a.D, BK, BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.V, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            nullptr, raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.part_m, a.part_s, a.tgt, a.N, a.V, a.v_offset};
   const CUtensorMap tmC{};  // the forward epilogue writes no tiles
-  if (pair) return launch_gemm2<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
@@ -1323,19 +1051,17 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
   CUtensorMap tmA, tmB;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
-  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, pair ? BN / 2 : BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
+  if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            a.counters ? a.counters + 0 : nullptr, raster_group(a.N * a.D * 2)};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
-                        a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld, pair ? 1 : 0};
+                        a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, a.dlogits, a.dtype, a.vc_len, a.N, a.vc_ld)) return cudaErrorInvalidValue;
-  if (pair) return launch_gemm2<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
@@ -1373,21 +1099,26 @@ cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
 namespace {
 
 template <typename T>
-cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t s) {
+cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, const PeerPush* push,
+                          cudaStream_t s) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tmA, tmB, tmC;
   const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
-  const bool pair = use_pair();
   if (!make_tmap(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
   int b3d = 0;
-  if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, (pair ? BN / 2 : BN) / 64, &b3d))
+  if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, (BN) / 64, &b3d))
     return cudaErrorInvalidValue;
   if (!make_tmap_acc2(&tmC, acc2, a.D, a.N)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
+  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.vc_len, BK), 1, 0, b3d,
            a.counters ? a.counters + 1 : nullptr, raster_group(a.N * a.vc_len * 2), 2};
   GradEEpi epi{a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile), (int)ceil_div(a.N, kRowBlock),
                (int)ceil_div(a.vc_len, kStatTile), accumulate ? 1 : 0, acc2, a.N, a.D};
-  if (pair) return launch_gemm2<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
+  if (push != nullptr) {
+    epi.push = 1;
+    epi.total_units = (unsigned)sc.units();
+    epi.peers = push->peers;
+    epi.layout = push->layout;
+  }
   return launch_gemm<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
@@ -1396,10 +1127,9 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tmA, tmB;
   int a3d = 0, b3d = 0;
-  const bool pair = use_pair();
   if (!make_tmap_mn(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BM / 64, &a3d)) return cudaErrorInvalidValue;
-  if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, (pair ? BN / 2 : BN) / 64, &b3d)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.vc_len, pair ? 2 * BM : BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
+  if (!make_tmap_mn(&tmB, a.e, bf16, a.D, a.N, a.D, (BN) / 64, &b3d)) return cudaErrorInvalidValue;
+  Sched sc{(int)ceil_div(a.vc_len, BM), (int)ceil_div(a.D, BN), (int)ceil_div(a.N, BK), 0, a3d, b3d,
            a.counters ? a.counters + 2 : nullptr, raster_group(a.N * a.D * 2)};
   GradCEpi<T> epi{static_cast<T*>(grad_c) + a.vc0 * a.D, a.scale,
                   a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
@@ -1408,16 +1138,15 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;
-  if (pair) return launch_gemm2<true, true>(tmA, tmB, tmC, sc, epi, bf16, s);
   return launch_gemm<true, true>(tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace
 
-cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, cudaStream_t s) {
+cudaError_t tc_grad_e(const BwdChunkArgs& a, float* acc2, bool accumulate, const PeerPush* push, cudaStream_t s) {
   if (a.N == 0 || a.D == 0) return cudaSuccess;
-  if (a.dtype == CCE_BF16) return grad_e_launch<__nv_bfloat16>(a, acc2, accumulate, s);
-  if (a.dtype == CCE_F16) return grad_e_launch<__half>(a, acc2, accumulate, s);
+  if (a.dtype == CCE_BF16) return grad_e_launch<__nv_bfloat16>(a, acc2, accumulate, push, s);
+  if (a.dtype == CCE_F16) return grad_e_launch<__half>(a, acc2, accumulate, push, s);
   return cudaErrorNotSupported;
 }
 

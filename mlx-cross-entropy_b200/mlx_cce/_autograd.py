@@ -11,18 +11,27 @@ deliberate:
   reference/_fused_backward.py:1618-1655, defines what they must be);
 * with a process group, ``c``/``bias`` are this rank's vocabulary shard and
   the per-row LSE / target logit are merged across ranks (one all-gather), and
-  grad_e is summed across ranks (one all-reduce).
+  grad_e is summed across ranks inside the library's backward over NVLink
+  peer memory (``cce_backward_peer``; ``_peer`` holds the exchange buffers).
+  ``CCE_GRAD_E_EXCHANGE=nccl`` in the environment selects the unfused
+  baseline instead: an fp32 grad_e partial per rank and one NCCL all-reduce.
 """
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
-from . import _ext
+from . import _ext, _peer
 from ._exchange import gather_shard_stats, sum_grad_e
 
 REDUCTIONS = ("none", "sum", "mean")
+
+
+def _peer_exchange() -> bool:
+    return os.environ.get("CCE_GRAD_E_EXCHANGE", "peer") != "nccl"
 
 
 class CCEFunction(torch.autograd.Function):
@@ -75,12 +84,14 @@ class CCEFunction(torch.autograd.Function):
         else:
             d_nll = (validf * (g / count)).contiguous()
         sharded = ctx.world > 1
+        peer = sharded and need_e and _peer_exchange()
+        pg = _peer.group_for(ctx.group, e.device, e.shape[0], e.shape[1], e.dtype) if peer else None
         ge, gc, gb = _ext.backward(e, c, targets, lse, d_nll, tile_max, bias, v_offset=ctx.v_offset,
                                    need_e=need_e, need_c=need_c, need_bias=need_b,
-                                   grad_e_f32=sharded and need_e,
+                                   grad_e_f32=sharded and need_e and not peer,
                                    filter_log_eps=ctx.filter_log_eps,
-                                   skip_stats=ctx.skip_stats)
-        if sharded and need_e:
+                                   skip_stats=ctx.skip_stats, peer_group=pg)
+        if sharded and need_e and not peer:
             ge = sum_grad_e(ge, ctx.group).to(e.dtype)
         if gb is not None:
             gb = gb.to(bias.dtype)

@@ -47,11 +47,24 @@ CCE_NO_FILTER = 16
 # ln(2^-12), csrc/cce/cce.metal:143 of the reference.
 FILTER_LOG_EPS = math.log(2.0 ** -12)
 
+CCE_PEER_MAX_WORLD = 16
+CCE_PEER_HANDLE_BYTES = 64
+CCE_PEER_WAIT_PUSH = 201
+CCE_PEER_WAIT_REDUCE = 202
+
 EXPORTED_SYMBOLS = (
     "cce_version", "cce_last_error", "cce_launch_count", "cce_device_status", "cce_num_stat_tiles",
     "cce_forward_workspace_bytes", "cce_forward", "cce_forward_noalloc", "cce_lse_combine",
     "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize", "cce_selftest_wait_timeout",
+    "cce_peer_buffer_bytes", "cce_peer_buffer_alloc", "cce_peer_buffer_open", "cce_peer_buffer_close",
+    "cce_peer_buffer_free", "cce_backward_peer",
 )
+
+
+class CcePeerGroup(ctypes.Structure):
+    """Mirror of ``CcePeerGroup`` (include/cce_b200.h)."""
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("wait_limit_ns", ctypes.c_int64),
+                ("bytes", ctypes.c_size_t), ("bases", ctypes.c_void_p * CCE_PEER_MAX_WORLD)]
 
 _DTYPE_CODE = {torch.float32: CCE_F32, torch.float16: CCE_F16, torch.bfloat16: CCE_BF16}
 
@@ -94,6 +107,20 @@ def _load():
     lib.cce_selftest_wait_timeout.argtypes = [c_i64, c_vp]
     lib.cce_dequantize.restype = c_int
     lib.cce_dequantize.argtypes = [c_vp, c_vp, c_vp, c_int, c_i64, c_i64, c_int, c_int, c_int, c_vp, c_vp]
+    lib.cce_peer_buffer_bytes.restype = c_sz
+    lib.cce_peer_buffer_bytes.argtypes = [c_i64, c_i64, c_int, c_int]
+    lib.cce_peer_buffer_alloc.restype = c_int
+    lib.cce_peer_buffer_alloc.argtypes = [c_sz, ctypes.POINTER(c_vp), c_vp]
+    lib.cce_peer_buffer_open.restype = c_int
+    lib.cce_peer_buffer_open.argtypes = [c_vp, ctypes.POINTER(c_vp)]
+    lib.cce_peer_buffer_close.restype = c_int
+    lib.cce_peer_buffer_close.argtypes = [c_vp]
+    lib.cce_peer_buffer_free.restype = c_int
+    lib.cce_peer_buffer_free.argtypes = [c_vp]
+    lib.cce_backward_peer.restype = c_int
+    lib.cce_backward_peer.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
+                                      c_i64, c_i64, c_int, c_int, c_f, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                      c_sz, ctypes.POINTER(CcePeerGroup), c_vp]
     return lib
 
 
@@ -286,13 +313,15 @@ def lse_combine(part_lse, part_tgt=None, stream=None):
 def backward(e, c, targets, lse, d_nll, tile_max, bias=None, *, v_offset: int = 0,
              need_e: bool = True, need_c: bool = False, need_bias: bool = False,
              grad_e_f32: bool = False, filter_log_eps: float = FILTER_LOG_EPS,
-             no_filter: bool = False, skip_stats=None, stream=None):
+             no_filter: bool = False, skip_stats=None, peer_group=None, stream=None):
     """Raw backward.  Returns (grad_e, grad_c, grad_bias); absent ones are None.
 
     grad_e is in e's dtype (fp32 with ``grad_e_f32``), grad_c in c's dtype,
-    grad_bias in fp32.
+    grad_bias in fp32.  With ``peer_group`` (a ``CcePeerGroup`` describing
+    the exchange buffers of a vocabulary-sharded group, see ``_peer``) this
+    runs ``cce_backward_peer``: grad_e comes back summed over the group.
     """
-    what = "cce_backward"
+    what = "cce_backward_peer" if peer_group is not None else "cce_backward"
     N, D = e.shape
     V = c.shape[0]
     dev = _require_cuda(what, e=e, c=c, targets=targets, lse=lse, d_nll=d_nll, tile_max=tile_max,
@@ -325,10 +354,17 @@ def backward(e, c, targets, lse, d_nll, tile_max, bias=None, *, v_offset: int = 
                                    or not skip_stats.is_cuda):
         raise ValueError(f"[{what}] skip_stats must be a CUDA int64 tensor with 2 entries")
     with _Timed("backward", _torch_stream(stream) if _timing is not None else None):
-        rc = lib.cce_backward(_ptr(e), _ptr(c), _ptr(bias), bdt, _ptr(targets), _ptr(lse),
-                              _ptr(d_nll), _ptr(tile_max), N, D, V, int(v_offset), dt, flags,
-                              float(filter_log_eps), _ptr(grad_e), _ptr(grad_c), _ptr(grad_b),
-                              _ptr(skip_stats), _ptr(ws), ws_bytes, _stream(stream))
+        if peer_group is not None:
+            rc = lib.cce_backward_peer(_ptr(e), _ptr(c), _ptr(bias), bdt, _ptr(targets), _ptr(lse),
+                                       _ptr(d_nll), _ptr(tile_max), N, D, V, int(v_offset), dt, flags,
+                                       float(filter_log_eps), _ptr(grad_e), _ptr(grad_c), _ptr(grad_b),
+                                       _ptr(skip_stats), _ptr(ws), ws_bytes, ctypes.byref(peer_group),
+                                       _stream(stream))
+        else:
+            rc = lib.cce_backward(_ptr(e), _ptr(c), _ptr(bias), bdt, _ptr(targets), _ptr(lse),
+                                  _ptr(d_nll), _ptr(tile_max), N, D, V, int(v_offset), dt, flags,
+                                  float(filter_log_eps), _ptr(grad_e), _ptr(grad_c), _ptr(grad_b),
+                                  _ptr(skip_stats), _ptr(ws), ws_bytes, _stream(stream))
     _check(rc, what)
     return grad_e, grad_c, grad_b
 

@@ -27,7 +27,7 @@ INCLUDE = REPO / "include"
 LIB_NAME = "libcce_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["cce_abi.cu", "aux_kernels.cu", "simt_kernels.cu", "tc_kernels.cu", "noalloc.cu"]
+SOURCES = ["cce_abi.cu", "aux_kernels.cu", "simt_kernels.cu", "tc_kernels.cu", "noalloc.cu", "peer.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -76,6 +76,37 @@ def test_error_codes_without_gpu_work():
     assert lib.cce_selftest_wait_timeout(3_000_000_000, None) == _ext.CCE_ERR_ARG
 
 
+def test_peer_buffer_layout_and_argument_checks():
+    """Exchange buffer of the sharded backward: a 4 KB control block, then
+    world x 2 fp32 receive slots of R rows (R = 128 * ceil(ceil(N / 128) /
+    world)), then R rows of the output dtype; each part 256-byte aligned."""
+    lib = _ext.lib
+
+    def expect(N, D, world, esize):
+        mt = -(-N // 128)
+        R = 128 * -(-mt // world)
+        up = lambda x: -(-x // 256) * 256
+        return 4096 + up(world * 2 * R * D * 4) + up(R * D * esize)
+
+    assert lib.cce_peer_buffer_bytes(4096, 4096, 8, _ext.CCE_BF16) == expect(4096, 4096, 8, 2)
+    assert lib.cce_peer_buffer_bytes(640, 256, 2, _ext.CCE_BF16) == expect(640, 256, 2, 2)
+    assert lib.cce_peer_buffer_bytes(200, 100, 2, _ext.CCE_F32) == expect(200, 100, 2, 4)
+    assert lib.cce_peer_buffer_bytes(32768, 8192, 8, _ext.CCE_BF16) == expect(32768, 8192, 8, 2)
+    assert lib.cce_peer_buffer_bytes(100, 64, 0, _ext.CCE_BF16) == 0
+    assert lib.cce_peer_buffer_bytes(100, 64, 17, _ext.CCE_BF16) == 0
+    # rejected before any CUDA call
+    args = [None, None, None, 0, None, None, None, None, 4, 8, 16, 0, 0, _ext.CCE_NEED_DE, -8.0,
+            None, None, None, None, None, 0]
+    assert lib.cce_backward_peer(*args, None, None) == _ext.CCE_ERR_ARG
+    g = _ext.CcePeerGroup()
+    g.rank, g.world = 0, 17
+    assert lib.cce_backward_peer(*args, ctypes.byref(g), None) == _ext.CCE_ERR_ARG
+    g.world = 2   # bases left NULL
+    assert lib.cce_backward_peer(*args, ctypes.byref(g), None) == _ext.CCE_ERR_ARG
+    assert b"NULL" in lib.cce_last_error()
+    assert lib.cce_peer_buffer_alloc(1 << 20, None, None) == _ext.CCE_ERR_ARG
+
+
 def test_python_api_rejects_cpu_tensors_and_bad_args():
     e = torch.randn(8, 16)
     c = torch.randn(32, 16)
