@@ -433,6 +433,7 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- eager timed region: per-call kernel times, launches, skipped blocks ----
     skip.zero_()
+    _ext.mma_flops(reset=True)
     launches0 = _ext.launch_count()
     _ext.set_timing(True)
     barrier()
@@ -451,6 +452,13 @@ def run_ours(args, rank, world, local_rank):
     fwd_avg = max_over_ranks(statistics.mean(fwd_ms)) if fwd_ms else float("nan")
     bwd_avg = max_over_ranks(statistics.mean(bwd_ms)) if bwd_ms else float("nan")
     skipped, total = skip.tolist()
+    # tensor-core work the kernels issued (filter-skipped blocks excluded), all ranks
+    mma = _ext.mma_flops(reset=True)
+    mma_t = torch.tensor([mma[k] / args.steps for k in ("forward", "dlogits", "grad_e", "grad_c")],
+                         dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(mma_t)
+    mma_step = dict(zip(("forward", "dlogits", "grad_e", "grad_c"), mma_t.tolist()))
 
     # ---- end-to-end through the public API with host buffers ----
     # Every step copies its inputs from pinned host memory and reads its loss
@@ -541,6 +549,11 @@ def run_ours(args, rank, world, local_rank):
             # against the 2.25 PFLOP/s dense-BF16 figure NVIDIA quotes per B200
             "pct_bf16_spec": tflops / (2250.0 * world),
             "flops_per_step": flops,
+            # what the tensor cores executed: the nominal 8 N V D minus the
+            # blocks the filter skipped (tile padding included)
+            "executed_flops_per_step": sum(mma_step.values()),
+            "executed_flops_by_kernel": mma_step,
+            "pct_bf16_peak_executed": sum(mma_step.values()) / (ms / 1e3) / 1e12 / (peak_burst * world),
             "skipped_blocks_frac": (skipped / total) if total else None,
             "fwd_ms": fwd_avg, "bwd_ms": bwd_avg,
             "roofline": {"bound": "tensor", "kernel": "forward (logits + online LSE)",

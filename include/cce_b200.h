@@ -79,6 +79,15 @@ CCE_API const char* cce_last_error(void);
  * reference. */
 CCE_API uint64_t cce_launch_count(void);
 
+/* Tensor-core work the library's GEMM kernels actually issued on the current
+ * device since the last reset: flops4[k] = 2 * 128 * 16 * (sum of N over the
+ * M = 128, K = 16 MMAs issued) for k = 0 forward, 1 dlogits, 2 grad_e,
+ * 3 grad_c.  Blocks skipped by the filter and MMA columns left out of a tile
+ * are not counted; padding of partial tiles is.  Synchronous; reset != 0
+ * clears the counters after reading.  Instrumentation only; no counterpart in
+ * the reference. */
+CCE_API int cce_mma_flops(uint64_t* flops4, int reset);
+
 /* Synchronous health check of the current device: CCE_OK, or CCE_ERR_CUDA if
  * a tensor-core kernel gave up on a pipeline wait after its time limit (it then
  * returns instead of hanging; its outputs are invalid).  reset != 0 clears the

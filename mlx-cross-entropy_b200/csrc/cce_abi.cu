@@ -124,15 +124,27 @@ struct BwdPlan {
 
 bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
 
+// CCE_BWD_CHUNK_ROWS=<rows> in the environment overrides the target rows per
+// backward vocabulary chunk (a tuning knob; the 1 GiB cap still applies).
+int64_t target_chunk_rows() {
+  static const int64_t v = [] {
+    const char* s = getenv("CCE_BWD_CHUNK_ROWS");
+    const long long r = s ? atoll(s) : 0;
+    return r >= 256 ? (int64_t)r : kDlTargetRows;
+  }();
+  return v;
+}
+
 BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {
   BwdPlan p{};
   p.tc = tc;
   const int64_t gran = tc ? 256 : 128;
   const int64_t elt = tc ? 2 : 4;
   const int64_t nrow = N > 0 ? N : 1;
-  int64_t budget = nrow * elt * kDlTargetRows;
+  const int64_t target = target_chunk_rows();
+  int64_t budget = nrow * elt * target;
   if (budget > kDlMaxBytes) budget = kDlMaxBytes;
-  if (budget < kDlMinBytes) budget = kDlMinBytes;
+  if (budget < kDlMinBytes && target == kDlTargetRows) budget = kDlMinBytes;
   int64_t vc = (budget / (nrow * elt)) / gran * gran;
   if (vc < gran) vc = gran;
   const int64_t vmax = cce::round_up(V > 0 ? V : 1, gran);
@@ -247,6 +259,13 @@ int cce_device_status(int reset) {
     return fail(CCE_ERR_CUDA, "a tensor-core kernel abandoned a pipeline wait after its time limit (code %d)", v);
   if (pv > 0)
     return fail(CCE_ERR_CUDA, "a grad_e exchange kernel gave up waiting for another rank (code %d)", pv);
+  return CCE_OK;
+}
+
+int cce_mma_flops(uint64_t* flops4, int reset) {
+  if (!flops4) return fail(CCE_ERR_ARG, "cce_mma_flops: NULL output");
+  if (cce::tc_read_mma_flops(flops4, reset != 0) != 0)
+    return fail(CCE_ERR_CUDA, "cce_mma_flops: could not read the device counters");
   return CCE_OK;
 }
 

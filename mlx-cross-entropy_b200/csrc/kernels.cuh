@@ -96,6 +96,9 @@ bool tc_backward_supported(const void* e, const void* c, int64_t D, int dtype);
 // Reads (and optionally clears) the tensor-core kernels' device status word:
 // 0 = ok, > 0 = code of a bounded wait that timed out, -1 = read failed.
 int tc_read_status(bool reset);
+// Executed MMA FLOPs per kernel kind (forward, dlogits, grad_e, grad_c) since
+// the last reset; 0 = ok, -1 = read failed.
+int tc_read_mma_flops(uint64_t* out4, bool reset);
 cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
 cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
 // acc2[2][N][D] fp32: each output tile's two K halves of this chunk are

@@ -73,6 +73,11 @@ constexpr uint32_t OUT_STAGE_BYTES = 4 * 4096;  // epilogue output staging, 4 KB
 constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
 constexpr int kPushWaitCode = 8;  // status code: a push unit's epilogue threads never all arrived
 
+// Executed tensor-core work per kernel kind (0 forward, 1 dlogits, 2 grad_e,
+// 3 grad_c): the sum of N over every issued M = 128, K = 16 MMA, added once
+// per CTA; FLOPs = 2 * 128 * 16 * sum.  Read by cce_mma_flops().
+__device__ unsigned long long g_mma_cols[4];
+
 // ---------------------------------------------------------------------------
 // helpers for the epilogues
 // ---------------------------------------------------------------------------
@@ -181,6 +186,7 @@ struct Stager {
 
 template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
+  static constexpr int kKind = 0;  // slot in g_mma_cols
   const int32_t* targets;
   const void* bias;
   float* tile_max;  // [ceil(V / kStatTile)][N]
@@ -263,6 +269,7 @@ struct FwdEpi {
 
 template <typename T, typename TB>
 struct DlogitsEpi {
+  static constexpr int kKind = 1;  // slot in g_mma_cols
   const int32_t* targets;
   const float* lse;
   const float* d_nll;
@@ -371,6 +378,7 @@ struct DlogitsEpi {
 // 16-byte stores over NVLink while the MMAs of the next units run; the last
 // unit raises the `pushed` flag on every rank.  The slabs are not written.
 struct GradEEpi {
+  static constexpr int kKind = 2;  // slot in g_mma_cols
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
   int64_t mask_ld;          // nVt
@@ -499,6 +507,7 @@ struct GradEEpi {
 
 template <typename T>
 struct GradCEpi {
+  static constexpr int kKind = 3;  // slot in g_mma_cols
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // activity table rows of the chunk's M tiles: [ceil(V/128)][mask_ld] words
@@ -728,6 +737,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      unsigned long long mma_cols = 0;  // sum of N over the issued M=128, K=16 MMAs
       // descriptors of stage 0, k-step 0; the start-address field (addr >> 4,
       // bits 0-13) is advanced by adding byte offsets >> 4
       const uint64_t adesc0 = A_MN ? smem_desc(smem_u32(sA), BOX_MN_BYTES, 1024)
@@ -773,6 +783,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         uint32_t fresh = 1;  // the tile's first MMA overwrites the accumulator
         for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
           const uint32_t km = epi.ksub_mask(mk, mb, nb, kb);  // K=16 steps to issue
+          mma_cols += (unsigned long long)(__popc(km & 0xFu) * kStatTile * n0);
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
           const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
@@ -795,6 +806,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
+      atomicAdd(&g_mma_cols[Epi::kKind], mma_cols);
     }
     __syncwarp();
   } else {
@@ -1177,6 +1189,17 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns, int code) {
 cudaError_t tc_selftest_wait(uint64_t limit_ns, int code, cudaStream_t s) {
   selftest_wait_kernel<<<1, 32, 0, s>>>(limit_ns, code);
   return launched();
+}
+
+int tc_read_mma_flops(uint64_t* out4, bool reset) {
+  unsigned long long v[4];
+  if (cudaMemcpyFromSymbol(v, g_mma_cols, sizeof(v)) != cudaSuccess) return -1;
+  for (int k = 0; k < 4; ++k) out4[k] = (uint64_t)v[k] * 2ull * 128ull * 16ull;
+  if (reset) {
+    const unsigned long long z[4] = {0, 0, 0, 0};
+    if (cudaMemcpyToSymbol(g_mma_cols, z, sizeof(z)) != cudaSuccess) return -1;
+  }
+  return 0;
 }
 
 int tc_read_status(bool reset) {

@@ -57,7 +57,7 @@ EXPORTED_SYMBOLS = (
     "cce_forward_workspace_bytes", "cce_forward", "cce_forward_noalloc", "cce_lse_combine",
     "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize", "cce_selftest_wait_timeout",
     "cce_peer_buffer_bytes", "cce_peer_buffer_alloc", "cce_peer_buffer_open", "cce_peer_buffer_close",
-    "cce_peer_buffer_free", "cce_backward_peer",
+    "cce_peer_buffer_free", "cce_backward_peer", "cce_mma_flops",
 )
 
 
@@ -117,6 +117,8 @@ def _load():
     lib.cce_peer_buffer_close.argtypes = [c_vp]
     lib.cce_peer_buffer_free.restype = c_int
     lib.cce_peer_buffer_free.argtypes = [c_vp]
+    lib.cce_mma_flops.restype = c_int
+    lib.cce_mma_flops.argtypes = [ctypes.POINTER(ctypes.c_uint64), c_int]
     lib.cce_backward_peer.restype = c_int
     lib.cce_backward_peer.argtypes = [c_vp, c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64,
                                       c_i64, c_i64, c_int, c_int, c_f, c_vp, c_vp, c_vp, c_vp, c_vp,
@@ -134,6 +136,14 @@ def version() -> int:
 def device_status(reset: bool = False):
     """Raise RuntimeError if a kernel abandoned a pipeline wait (synchronous)."""
     _check(lib.cce_device_status(1 if reset else 0), "cce_device_status")
+
+
+def mma_flops(reset: bool = False):
+    """Executed tensor-core FLOPs since the last reset (synchronous):
+    {"forward", "dlogits", "grad_e", "grad_c"} -> FLOPs."""
+    out = (ctypes.c_uint64 * 4)()
+    _check(lib.cce_mma_flops(out, 1 if reset else 0), "cce_mma_flops")
+    return dict(zip(("forward", "dlogits", "grad_e", "grad_c"), (int(x) for x in out)))
 
 
 def launch_count() -> int:

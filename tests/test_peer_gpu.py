@@ -135,7 +135,8 @@ def test_missing_rank_times_out_and_the_context_survives():
         raw_backward(e, c, t, peer_group=group(buf, world=2, rank=0, wait_ms=50))
         with pytest.raises(RuntimeError, match=f"code {_ext.CCE_PEER_WAIT_PUSH}"):
             _ext.device_status()
-        _ext.device_status(reset=True)   # cleared
+        with pytest.raises(RuntimeError, match=f"code {_ext.CCE_PEER_WAIT_PUSH}"):
+            _ext.device_status(reset=True)   # reports, then clears
         _ext.device_status()
     finally:
         buf.close()
