@@ -233,15 +233,19 @@ CCE_API int cce_dequantize(const uint32_t* wq, const void* scales, const void* b
  * stores instead of a collective library.
  *
  * Every rank of a group (one process per GPU of one node) allocates one
- * exchange buffer with cce_peer_buffer_alloc, sends its IPC handle to every
- * other rank (any host-side channel: the caller's process group), opens the
- * others' handles with cce_peer_buffer_open, and passes all of them in a
- * CcePeerGroup.  Buffers are allocated once per group, not per call (this is
- * set-up, the only place this library allocates device memory).
+ * exchange buffer with cce_peer_buffer_alloc, which returns a POSIX file
+ * descriptor of the buffer's physical memory; sends it to every other rank of
+ * the node (file descriptors travel between processes only through a Unix
+ * socket, SCM_RIGHTS); maps the others' buffers with cce_peer_buffer_open;
+ * and passes all of them in a CcePeerGroup.  The buffers are driver
+ * virtual-memory allocations mapped with access for each rank's own device
+ * only: no context-wide peer access is turned on, so the process's other
+ * allocations stay as cheap as without the group.  Buffers are allocated once
+ * per group, not per call (this is set-up, the only place this library
+ * allocates device memory).
  * --------------------------------------------------------------------------- */
 
 #define CCE_PEER_MAX_WORLD    16
-#define CCE_PEER_HANDLE_BYTES 64   /* a cudaIpcMemHandle_t */
 /* cce_device_status codes of the exchange's bounded waits */
 #define CCE_PEER_WAIT_PUSH    201  /* a rank's partial grad_e never arrived      */
 #define CCE_PEER_WAIT_REDUCE  202  /* a rank's reduced rows never became ready   */
@@ -259,14 +263,19 @@ typedef struct CcePeerGroup {
  * result written in out_dtype (CCE_F32 / F16 / BF16). */
 CCE_API size_t cce_peer_buffer_bytes(int64_t N, int64_t D, int world, int out_dtype);
 
-/* Allocates a zero-initialised exchange buffer on the current device and
- * writes its IPC handle (CCE_PEER_HANDLE_BYTES bytes) to ipc_handle. */
-CCE_API int cce_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
-/* Maps another rank's buffer into this process (enables peer access). */
-CCE_API int cce_peer_buffer_open(const void* ipc_handle, void** ptr);
-/* Unmaps a buffer opened with cce_peer_buffer_open. */
+/* Allocates a zero-initialised exchange buffer of at least `bytes` on the
+ * current device, maps it at *ptr, and writes to *fd a new POSIX file
+ * descriptor that shares it (the caller sends it to the other ranks and
+ * closes it). */
+CCE_API int cce_peer_buffer_alloc(size_t bytes, void** ptr, int* fd);
+/* Maps another rank's buffer (its descriptor, received in this process, and
+ * the same `bytes`) at *ptr with access for the current device.  The caller
+ * may close `fd` afterwards. */
+CCE_API int cce_peer_buffer_open(int fd, size_t bytes, void** ptr);
+/* Unmaps a buffer mapped with cce_peer_buffer_open. */
 CCE_API int cce_peer_buffer_close(void* ptr);
-/* Frees a buffer from cce_peer_buffer_alloc (after every rank closed it). */
+/* Unmaps and releases a buffer from cce_peer_buffer_alloc (its memory lives
+ * on while another process still maps it). */
 CCE_API int cce_peer_buffer_free(void* ptr);
 
 /*

@@ -11,7 +11,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "kernels.cuh"
 
@@ -231,6 +233,138 @@ int side_streams(SideStreams** out) {
     ss = n;
   }
   *out = &ss;
+  return CCE_OK;
+}
+
+// ---- exchange buffers: driver virtual-memory API ----
+//
+// Each buffer is a physical allocation (cuMemCreate) exportable as a POSIX
+// file descriptor, mapped into a reserved virtual range with access for the
+// local device only.  A peer process imports the descriptor and maps the same
+// physical memory into its own range, again with access for its own device.
+// Unlike CUDA IPC this turns on no context-wide peer access, which would make
+// every later cudaMalloc of the process map its memory into the peer device
+// (measured: ~5 ms per new allocator segment on B200).
+
+struct VmmApi {
+  using CreateFn = CUresult (*)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long);
+  using ReleaseFn = CUresult (*)(CUmemGenericAllocationHandle);
+  using ReserveFn = CUresult (*)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
+  using AddrFreeFn = CUresult (*)(CUdeviceptr, size_t);
+  using MapFn = CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
+  using UnmapFn = CUresult (*)(CUdeviceptr, size_t);
+  using SetAccessFn = CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
+  using ExportFn = CUresult (*)(void*, CUmemGenericAllocationHandle, CUmemAllocationHandleType, unsigned long long);
+  using ImportFn = CUresult (*)(CUmemGenericAllocationHandle*, void*, CUmemAllocationHandleType);
+  using GranFn = CUresult (*)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags);
+  CreateFn create = nullptr;
+  ReleaseFn release = nullptr;
+  ReserveFn reserve = nullptr;
+  AddrFreeFn addr_free = nullptr;
+  MapFn map = nullptr;
+  UnmapFn unmap = nullptr;
+  SetAccessFn set_access = nullptr;
+  ExportFn export_fd = nullptr;
+  ImportFn import_fd = nullptr;
+  GranFn granularity = nullptr;
+  bool ok = false;
+};
+
+template <typename Fn>
+Fn entry(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
+const VmmApi& vmm_api() {
+  static const VmmApi api = [] {
+    VmmApi a;
+    a.create = entry<VmmApi::CreateFn>("cuMemCreate");
+    a.release = entry<VmmApi::ReleaseFn>("cuMemRelease");
+    a.reserve = entry<VmmApi::ReserveFn>("cuMemAddressReserve");
+    a.addr_free = entry<VmmApi::AddrFreeFn>("cuMemAddressFree");
+    a.map = entry<VmmApi::MapFn>("cuMemMap");
+    a.unmap = entry<VmmApi::UnmapFn>("cuMemUnmap");
+    a.set_access = entry<VmmApi::SetAccessFn>("cuMemSetAccess");
+    a.export_fd = entry<VmmApi::ExportFn>("cuMemExportToShareableHandle");
+    a.import_fd = entry<VmmApi::ImportFn>("cuMemImportFromShareableHandle");
+    a.granularity = entry<VmmApi::GranFn>("cuMemGetAllocationGranularity");
+    a.ok = a.create && a.release && a.reserve && a.addr_free && a.map && a.unmap && a.set_access &&
+           a.export_fd && a.import_fd && a.granularity;
+    return a;
+  }();
+  return api;
+}
+
+CUmemAllocationProp device_prop(int dev) {
+  CUmemAllocationProp prop;
+  memset(&prop, 0, sizeof(prop));
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = dev;
+  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return prop;
+}
+
+void unmap(const VmmApi& api, CUdeviceptr va, size_t size) {
+  api.unmap(va, size);
+  api.addr_free(va, size);
+}
+
+// Reserve a range, map `h` into it and give the local device read/write access.
+int map_local(const VmmApi& api, CUmemGenericAllocationHandle h, size_t size, int dev, CUdeviceptr* out) {
+  CUdeviceptr va = 0;
+  CUresult r = api.reserve(&va, size, 0, 0, 0);
+  if (r != CUDA_SUCCESS) return fail(CCE_ERR_CUDA, "cuMemAddressReserve of %zu bytes failed (%d)", size, (int)r);
+  if ((r = api.map(va, size, 0, h, 0)) != CUDA_SUCCESS) {
+    api.addr_free(va, size);
+    return fail(CCE_ERR_CUDA, "cuMemMap failed (%d)", (int)r);
+  }
+  CUmemAccessDesc acc;
+  memset(&acc, 0, sizeof(acc));
+  acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  acc.location.id = dev;
+  acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  if ((r = api.set_access(va, size, &acc, 1)) != CUDA_SUCCESS) {
+    unmap(api, va, size);
+    return fail(CCE_ERR_CUDA, "cuMemSetAccess failed (%d)", (int)r);
+  }
+  *out = va;
+  return CCE_OK;
+}
+
+// Mapped exchange buffers of this process: base address -> (handle, size).
+struct Mapping {
+  CUmemGenericAllocationHandle handle;
+  size_t size;
+};
+std::mutex g_maps_mu;
+std::unordered_map<uintptr_t, Mapping> g_maps;
+
+void remember(CUdeviceptr va, CUmemGenericAllocationHandle h, size_t size) {
+  std::lock_guard<std::mutex> lock(g_maps_mu);
+  g_maps[(uintptr_t)va] = Mapping{h, size};
+}
+
+int forget_and_unmap(void* ptr, const char* what) {
+  Mapping m;
+  {
+    std::lock_guard<std::mutex> lock(g_maps_mu);
+    auto it = g_maps.find(reinterpret_cast<uintptr_t>(ptr));
+    if (it == g_maps.end()) return fail(CCE_ERR_ARG, "%s: %p is not a mapped exchange buffer", what, ptr);
+    m = it->second;
+    g_maps.erase(it);
+  }
+  const VmmApi& api = vmm_api();
+  const CUdeviceptr va = reinterpret_cast<CUdeviceptr>(ptr);
+  const CUresult r1 = api.unmap(va, m.size);
+  const CUresult r2 = api.addr_free(va, m.size);
+  const CUresult r3 = api.release(m.handle);
+  if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS || r3 != CUDA_SUCCESS)
+    return fail(CCE_ERR_CUDA, "%s: unmapping failed (%d, %d, %d)", what, (int)r1, (int)r2, (int)r3);
   return CCE_OK;
 }
 
@@ -521,41 +655,82 @@ size_t cce_peer_buffer_bytes(int64_t N, int64_t D, int world, int out_dtype) {
   return cce::peer::make_layout(N, D, world, (int)dtype_size(out_dtype)).bytes;
 }
 
-int cce_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
-  if (!ptr || !ipc_handle) return fail(CCE_ERR_ARG, "cce_peer_buffer_alloc: NULL output pointer");
+int cce_peer_buffer_alloc(size_t bytes, void** ptr, int* fd) {
+  if (!ptr || !fd) return fail(CCE_ERR_ARG, "cce_peer_buffer_alloc: NULL output pointer");
   if (bytes < cce::peer::kCtrlBytes) return fail(CCE_ERR_ARG, "cce_peer_buffer_alloc: %zu bytes is too small", bytes);
   int rc = check_arch();
   if (rc) return rc;
-  void* p = nullptr;
-  CCE_CUDA_CHECK(cudaMalloc(&p, bytes), "cce_peer_buffer_alloc cudaMalloc");
-  cudaError_t err = cudaMemset(p, 0, bytes);
-  if (err == cudaSuccess) err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
-  if (err != cudaSuccess) {
-    cudaFree(p);
-    return cuda_fail(err, "cce_peer_buffer_alloc");
+  const VmmApi& api = vmm_api();
+  if (!api.ok) return fail(CCE_ERR_CUDA, "cce_peer_buffer_alloc: the driver's virtual-memory API is unavailable");
+  int dev = 0;
+  CCE_CUDA_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+  CUmemAllocationProp prop = device_prop(dev);
+  size_t gran = 0;
+  CUresult r = api.granularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED);
+  if (r != CUDA_SUCCESS || gran == 0) return fail(CCE_ERR_CUDA, "cuMemGetAllocationGranularity failed (%d)", (int)r);
+  const size_t size = (bytes + gran - 1) / gran * gran;
+  CUmemGenericAllocationHandle h = 0;
+  if ((r = api.create(&h, size, &prop, 0)) != CUDA_SUCCESS)
+    return fail(CCE_ERR_CUDA, "cuMemCreate of %zu bytes failed (%d)", size, (int)r);
+  CUdeviceptr va = 0;
+  rc = map_local(api, h, size, dev, &va);
+  if (rc) {
+    api.release(h);
+    return rc;
   }
-  *ptr = p;
+  int shared = -1;
+  if ((r = api.export_fd(&shared, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0)) != CUDA_SUCCESS) {
+    unmap(api, va, size);
+    api.release(h);
+    return fail(CCE_ERR_CUDA, "cuMemExportToShareableHandle failed (%d)", (int)r);
+  }
+  // zero the whole buffer (the control block above all) before any rank maps it
+  cudaError_t err = cudaMemset(reinterpret_cast<void*>(va), 0, size);
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) {
+    unmap(api, va, size);
+    api.release(h);
+    return cuda_fail(err, "cce_peer_buffer_alloc memset");
+  }
+  remember(va, h, size);
+  *ptr = reinterpret_cast<void*>(va);
+  *fd = shared;
   return CCE_OK;
 }
 
-int cce_peer_buffer_open(const void* ipc_handle, void** ptr) {
-  if (!ptr || !ipc_handle) return fail(CCE_ERR_ARG, "cce_peer_buffer_open: NULL pointer");
-  cudaIpcMemHandle_t h;
-  memcpy(&h, ipc_handle, sizeof(h));
-  CCE_CUDA_CHECK(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cce_peer_buffer_open");
+int cce_peer_buffer_open(int fd, size_t bytes, void** ptr) {
+  if (!ptr || fd < 0) return fail(CCE_ERR_ARG, "cce_peer_buffer_open: NULL pointer or bad descriptor");
+  const VmmApi& api = vmm_api();
+  if (!api.ok) return fail(CCE_ERR_CUDA, "cce_peer_buffer_open: the driver's virtual-memory API is unavailable");
+  int dev = 0;
+  CCE_CUDA_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+  CUmemAllocationProp prop = device_prop(dev);
+  size_t gran = 0;
+  CUresult r = api.granularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED);
+  if (r != CUDA_SUCCESS || gran == 0) return fail(CCE_ERR_CUDA, "cuMemGetAllocationGranularity failed (%d)", (int)r);
+  const size_t size = (bytes + gran - 1) / gran * gran;
+  CUmemGenericAllocationHandle h = 0;
+  r = api.import_fd(&h, reinterpret_cast<void*>(static_cast<uintptr_t>(fd)), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+  if (r != CUDA_SUCCESS) return fail(CCE_ERR_CUDA, "cuMemImportFromShareableHandle failed (%d)", (int)r);
+  CUdeviceptr va = 0;
+  int rc = map_local(api, h, size, dev, &va);
+  if (rc) {
+    api.release(h);
+    return rc;
+  }
+  remember(va, h, size);
+  *ptr = reinterpret_cast<void*>(va);
   return CCE_OK;
 }
 
 int cce_peer_buffer_close(void* ptr) {
   if (!ptr) return CCE_OK;
-  CCE_CUDA_CHECK(cudaIpcCloseMemHandle(ptr), "cce_peer_buffer_close");
-  return CCE_OK;
+  return forget_and_unmap(ptr, "cce_peer_buffer_close");
 }
 
 int cce_peer_buffer_free(void* ptr) {
   if (!ptr) return CCE_OK;
-  CCE_CUDA_CHECK(cudaFree(ptr), "cce_peer_buffer_free");
-  return CCE_OK;
+  return forget_and_unmap(ptr, "cce_peer_buffer_free");
 }
 
 int cce_dequantize(const uint32_t* wq, const void* scales, const void* biases, int scale_dtype, int64_t rows,

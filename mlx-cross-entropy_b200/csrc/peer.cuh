@@ -3,7 +3,8 @@
 // exchange kernels (peer.cu).
 //
 // Every rank owns one buffer, allocated once per process group and mapped into
-// every other rank's process (CUDA IPC), so each rank reaches every buffer
+// every other rank's process (driver virtual memory shared through a file
+// descriptor), so each rank reaches every buffer
 // with plain loads and stores over NVLink:
 //
 //   [0, 4 KB)        control block (flags and counters, below)

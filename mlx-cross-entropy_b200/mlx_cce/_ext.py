@@ -48,7 +48,6 @@ CCE_NO_FILTER = 16
 FILTER_LOG_EPS = math.log(2.0 ** -12)
 
 CCE_PEER_MAX_WORLD = 16
-CCE_PEER_HANDLE_BYTES = 64
 CCE_PEER_WAIT_PUSH = 201
 CCE_PEER_WAIT_REDUCE = 202
 
@@ -110,9 +109,9 @@ def _load():
     lib.cce_peer_buffer_bytes.restype = c_sz
     lib.cce_peer_buffer_bytes.argtypes = [c_i64, c_i64, c_int, c_int]
     lib.cce_peer_buffer_alloc.restype = c_int
-    lib.cce_peer_buffer_alloc.argtypes = [c_sz, ctypes.POINTER(c_vp), c_vp]
+    lib.cce_peer_buffer_alloc.argtypes = [c_sz, ctypes.POINTER(c_vp), ctypes.POINTER(c_int)]
     lib.cce_peer_buffer_open.restype = c_int
-    lib.cce_peer_buffer_open.argtypes = [c_vp, ctypes.POINTER(c_vp)]
+    lib.cce_peer_buffer_open.argtypes = [c_int, c_sz, ctypes.POINTER(c_vp)]
     lib.cce_peer_buffer_close.restype = c_int
     lib.cce_peer_buffer_close.argtypes = [c_vp]
     lib.cce_peer_buffer_free.restype = c_int

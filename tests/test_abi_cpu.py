@@ -105,6 +105,7 @@ def test_peer_buffer_layout_and_argument_checks():
     assert lib.cce_backward_peer(*args, ctypes.byref(g), None) == _ext.CCE_ERR_ARG
     assert b"NULL" in lib.cce_last_error()
     assert lib.cce_peer_buffer_alloc(1 << 20, None, None) == _ext.CCE_ERR_ARG
+    assert lib.cce_peer_buffer_open(-1, 1 << 20, None) == _ext.CCE_ERR_ARG
 
 
 def test_python_api_rejects_cpu_tensors_and_bad_args():

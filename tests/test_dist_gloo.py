@@ -138,3 +138,48 @@ def test_failed_rank_surfaces_as_error_not_hang():
             p.kill()
     assert results[1] == "RuntimeError"
     assert results[0] != "no error"
+
+
+def _worker_fd_exchange(rank, world, port, q):
+    """Ranks send each other a descriptor of a file holding their rank id, with
+    the code the GPU exchange buffers use (mlx_cce._peer.PeerGroup._exchange_fds)."""
+    import sys
+    from pathlib import Path
+    repo = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(repo / "mlx-cross-entropy_b200"))
+    from mlx_cce import _peer
+    try:
+        _init(rank, world, port)
+        pg = _peer.PeerGroup(dist.group.WORLD, torch.device("cpu"))
+        fd = os.memfd_create(f"cce-test-{rank}")
+        os.write(fd, b"rank %d" % rank)
+        got = _peer.PeerGroup._exchange_fds(pg, fd)
+        os.close(fd)
+        seen = {}
+        for r, rfd in got.items():
+            seen[r] = os.pread(rfd, 16, 0).decode()
+            os.close(rfd)
+        q.put((rank, "ok", seen))
+    except Exception as exc:  # reported through the queue
+        q.put((rank, "error", repr(exc)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3, 12])
+def test_exchange_buffer_descriptors_reach_every_rank(world):
+    """12 ranks exceed the datagram queue length of 10: the receiving thread
+    must drain while the sends go out."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_fd_exchange, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, status, seen in out:
+        assert status == "ok", (rank, seen)
+        assert seen == {r: f"rank {r}" for r in range(world) if r != rank}

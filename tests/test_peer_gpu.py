@@ -17,6 +17,7 @@ what one process can:
 """
 
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -35,9 +36,9 @@ class Buffer:
     """One exchange buffer from cce_peer_buffer_alloc, freed on close()."""
 
     def __init__(self, nbytes):
-        handle = (ctypes.c_char * _ext.CCE_PEER_HANDLE_BYTES)()
-        ptr = ctypes.c_void_p()
-        _ext._check(_ext.lib.cce_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle), "alloc")
+        ptr, fd = ctypes.c_void_p(), ctypes.c_int(-1)
+        _ext._check(_ext.lib.cce_peer_buffer_alloc(nbytes, ctypes.byref(ptr), ctypes.byref(fd)), "alloc")
+        os.close(fd.value)   # no other process maps it
         self.ptr, self.nbytes = ptr.value, nbytes
 
     def close(self):
