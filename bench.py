@@ -592,6 +592,66 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_quantized(args):
+    """Frozen quantised head (the reference's mlx-lm LoRA recipe, README.md:84-95):
+    tokens/s of fwd + bwd (grad_e only) with the classifier kept group-quantised
+    in HBM, beside the same step on the dense head with c frozen.  Eager steps,
+    CUDA events on the launching stream; one GPU."""
+    import mlx_cce
+    from mlx_cce import synthetic
+    from mlx_cce.quantized import linear_cross_entropy_quantized, quantize
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    e_cpu, c_cpu, t_cpu, b_cpu, go_cpu, w = synthetic.make_inputs(args.config, N=args.N, V=args.V, D=args.D)
+    N, D = e_cpu.reshape(-1, e_cpu.shape[-1]).shape
+    e = e_cpu.reshape(N, D).to(dev)
+    t = t_cpu.reshape(N).to(dev)
+    c = c_cpu.to(dev)
+    q = quantize(c, args.group_size, args.quantized_bits)
+    V = c.shape[0]
+    c_deq = q.dequantize(c.dtype)          # the dense head the quantised one stands for
+    del c
+
+    def dense():
+        ei = e.detach().requires_grad_(True)
+        loss = mlx_cce.linear_cross_entropy(ei, c_deq, t, reduction=w.reduction)
+        (loss.sum() if w.reduction == "none" else loss).backward()
+
+    def quant():
+        ei = e.detach().requires_grad_(True)
+        loss = linear_cross_entropy_quantized(ei, q, t, reduction=w.reduction)
+        (loss.sum() if w.reduction == "none" else loss).backward()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    dense_ms = timed(dense)
+    quant_ms = timed(quant)
+    line = {
+        "metric": "CCE fwd+bwd tokens/s with a frozen quantised classifier", "value": N / (quant_ms / 1e3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": quant_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded, see mlx_cce/synthetic.py)",
+        "config": dict(workload_config(w, N, D, V, 1, args.N is not None or args.V is not None),
+                       classifier=f"{args.quantized_bits}-bit affine, groups of {args.group_size}, frozen",
+                       gradients="grad_e only"),
+        "dense_frozen_ms_per_step": dense_ms,
+        "quantized_over_dense": quant_ms / dense_ms,
+        "timing": "eager steps, CUDA events",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -608,6 +668,9 @@ def main():
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the check of one step against the float64 oracle")
     ap.add_argument("--no-graph", action="store_true", help="time eager steps instead of graph replays")
+    ap.add_argument("--quantized-bits", type=int, default=0,
+                    help="time a frozen classifier quantised to 2/4/8 bits beside the dense frozen one")
+    ap.add_argument("--group-size", type=int, default=64, help="quantisation group size")
     ap.add_argument("--N", type=int, default=None, help="scaled-down rows (profiling captures)")
     ap.add_argument("--V", type=int, default=None, help="scaled-down vocabulary (profiling captures)")
     ap.add_argument("--D", type=int, default=None, help="scaled-down hidden size (profiling captures)")
@@ -619,6 +682,10 @@ def main():
     local_rank = env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.quantized_bits:
+        if world > 1:
+            raise SystemExit("--quantized-bits runs on one GPU")
+        return run_quantized(args)
     return run_ours(args, rank, world, local_rank)
 
 

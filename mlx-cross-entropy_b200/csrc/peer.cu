@@ -202,9 +202,14 @@ __global__ void gather_kernel(Peers P, Layout L, int64_t N, int64_t D, TO* __res
   }
 }
 
+// At most 2 CTAs of 256 threads per SM: these kernels run on the grad_e
+// stream, which has the higher priority, while the persistent grad_c kernel
+// of the same chunk waits for SMs; two of them (2 x ~14K registers) still
+// leave room on an SM for one grad_c CTA (~14K registers, 225 KB of shared
+// memory), so waiting on another rank never keeps grad_c off the GPU.
 int grid_for(int64_t items) {
   const int64_t g = ceil_div(items > 0 ? items : 1, 256);
-  return (int)(g < 592 ? g : 592);  // at most 4 CTAs of 256 threads per SM
+  return (int)(g < 296 ? g : 296);
 }
 
 }  // namespace

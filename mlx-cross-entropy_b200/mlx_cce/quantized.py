@@ -29,7 +29,7 @@ from . import _ext
 from ._autograd import REDUCTIONS, sanitize_targets
 from ._ext import FILTER_LOG_EPS
 
-__all__ = ["QuantizedClassifier", "linear_cross_entropy_quantized"]
+__all__ = ["QuantizedClassifier", "linear_cross_entropy_quantized", "quantize"]
 
 
 class QuantizedClassifier(NamedTuple):
@@ -50,6 +50,34 @@ class QuantizedClassifier(NamedTuple):
         v1 = self.weight.shape[0] if v1 is None else v1
         return _ext.dequantize(self.weight[v0:v1], self.scales[v0:v1], self.biases[v0:v1],
                                self.group_size, self.bits, dtype, out=out)
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4) -> QuantizedClassifier:
+    """Affine group quantisation of a [V, D] matrix, on w's device (mx.quantize's format).
+
+    Per group of ``group_size`` values along D: bias = min, scale =
+    (max - min) / (2^bits - 1) (1 for a constant group), q = round((w - bias) /
+    scale) clipped to [0, 2^bits); q packed 32 / bits per uint32, low bits
+    first.  scales / biases keep w's dtype (float32 for float32 input).
+    """
+    if bits not in (2, 4, 8) or group_size not in (32, 64, 128):
+        raise ValueError(f"bits must be 2, 4 or 8 and group_size 32, 64 or 128, got {bits}, {group_size}")
+    V, D = w.shape
+    if D % group_size != 0:
+        raise ValueError(f"D={D} is not a multiple of group_size={group_size}")
+    g = w.float().reshape(V, D // group_size, group_size)
+    lo = g.amin(dim=2)
+    scale = (g.amax(dim=2) - lo) / float((1 << bits) - 1)
+    scale = torch.where(scale == 0, torch.ones_like(scale), scale)
+    q = torch.clamp(torch.round((g - lo[..., None]) / scale[..., None]), 0, (1 << bits) - 1)
+    per = 32 // bits
+    q = q.to(torch.int64).reshape(V, D // per, per)
+    shifts = torch.arange(per, device=w.device, dtype=torch.int64) * bits
+    words = (q << shifts).sum(dim=2)                        # < 2^32
+    words = torch.where(words >= (1 << 31), words - (1 << 32), words).to(torch.int32)
+    sdt = w.dtype if w.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float32
+    return QuantizedClassifier(words.contiguous(), scale.to(sdt).contiguous(), lo.to(sdt).contiguous(),
+                               group_size, bits)
 
 
 def _chunks(V: int, rows: int):

@@ -56,3 +56,19 @@ def test_quantized_api_validation():
         mlx_cce.linear_cross_entropy_quantized(torch.randn(3, 32), q, t)
     with pytest.raises(ValueError, match="CUDA tensor"):
         _ext.dequantize(wq, s, s, 64, 4, torch.bfloat16)
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("group_size", [32, 64, 128])
+def test_torch_quantize_matches_the_oracle_format(bits, group_size):
+    """mlx_cce.quantized.quantize (runs on any torch device) packs the same
+    words, scales and biases as the oracle's restatement of MLX's affine format."""
+    from mlx_cce.quantized import quantize
+    w = torch.randn(48, 256, generator=torch.Generator().manual_seed(bits * group_size))
+    w[3, :group_size] = 0.25   # a constant group: scale 1
+    q = quantize(w, group_size, bits)
+    wq, scales, biases = O.quantize_affine(w.numpy(), group_size, bits)
+    assert q.weight.dtype == torch.int32
+    np.testing.assert_array_equal(q.weight.numpy().view(np.uint32), wq)
+    np.testing.assert_allclose(q.scales.numpy(), scales, rtol=1e-6)
+    np.testing.assert_allclose(q.biases.numpy(), biases, rtol=1e-6)
