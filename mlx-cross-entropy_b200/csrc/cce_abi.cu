@@ -79,13 +79,17 @@ int cuda_fail(cudaError_t err, const char* where) {
   } while (0)
 
 constexpr size_t kAlign = 256;
-// dlogits chunk buffer: aim for 16384 vocabulary rows per chunk (few launches,
-// few kernel-to-kernel transitions, little grad_e accumulator traffic) within
-// 1 GiB, and never below 128 MiB.  (32768-row chunks, or two buffers so that a
-// chunk's dlogits overlap the previous chunk's grads, measured no faster.)
-constexpr int64_t kDlTargetRows = 16384;
+// dlogits chunk buffer: aim for 32768 vocabulary rows per chunk, within 1 GiB,
+// and never below 512 MiB.  Every chunk costs three kernel launches whatever
+// its work (~70 us at N = 2048 when the filter rejects nearly every block), so
+// small N gets long chunks: measured on B200, config 4 (N = 2048) backward
+// 1.44 ms in 8 chunks -> 1.01 ms in 2, config 2 (N = 1024) 0.65 -> 0.52 ms in
+// one; config 3 (N = 4096) 8.71 ms at 16384 rows, 8.35 at 32768, 8.42 at
+// 65536, 8.62 at 131072.  (Two buffers, so that a chunk's dlogits overlap the
+// previous chunk's grads, measured no faster.)
+constexpr int64_t kDlTargetRows = 32768;
 constexpr int64_t kDlMaxBytes = 1ll << 30;
-constexpr int64_t kDlMinBytes = 128ll << 20;
+constexpr int64_t kDlMinBytes = 512ll << 20;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -127,14 +131,13 @@ struct BwdPlan {
 bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
 
 // CCE_BWD_CHUNK_ROWS=<rows> in the environment overrides the target rows per
-// backward vocabulary chunk (a tuning knob; the 1 GiB cap still applies).
+// backward vocabulary chunk (a tuning knob, also used by the tests to force
+// several chunks; read on every call; the 1 GiB cap still applies, the 512 MiB
+// floor does not).
 int64_t target_chunk_rows() {
-  static const int64_t v = [] {
-    const char* s = getenv("CCE_BWD_CHUNK_ROWS");
-    const long long r = s ? atoll(s) : 0;
-    return r >= 256 ? (int64_t)r : kDlTargetRows;
-  }();
-  return v;
+  const char* s = getenv("CCE_BWD_CHUNK_ROWS");
+  const long long r = s ? atoll(s) : 0;
+  return r >= 256 ? (int64_t)r : kDlTargetRows;
 }
 
 BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {

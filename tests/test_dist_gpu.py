@@ -55,6 +55,7 @@ def _worker(rank, world, port, mode, q):
     sys.path.insert(0, str(repo / "mlx-cross-entropy_b200"))
     sys.path.insert(0, str(repo))
     os.environ["CCE_GRAD_E_EXCHANGE"] = mode
+    os.environ["CCE_BWD_CHUNK_ROWS"] = "16384"   # several vocabulary chunks per rank in the big case
     import torch.distributed as dist
     import mlx_cce
     from mlx_cce import distributed as mdist, _peer

@@ -279,14 +279,16 @@ def test_ragged_shapes(N, D, V, dtype):
     check(run(e, c, t), oracle(e, c, t), dtype)
 
 
-def test_multichunk_fp16_bias_ragged():
-    """N = 4200 rows (not a multiple of 128) makes the backward take 16384-row
-    vocabulary chunks: V = 36000 gives three (the last one 3232 rows, not a
-    multiple of 64), so grad_e's two accumulator slabs are stored, then
-    reduce-added, and grad_c's MN-major operand falls back to 2-D boxes in the
-    last chunk.  fp16 with an fp32 bias, 10% ignored rows, reduction 'sum'.
-    Against the float64 oracle: the loss over all rows, dE on sampled rows, dC
-    and dBias on sampled vocabulary rows (both ends of every chunk)."""
+def test_multichunk_fp16_bias_ragged(monkeypatch):
+    """N = 4200 rows (not a multiple of 128) with 16384-row vocabulary chunks
+    (forced through CCE_BWD_CHUNK_ROWS; the default rule would take one chunk
+    here): V = 36000 gives three (the last one 3232 rows, not a multiple of
+    64), so grad_e's two accumulator slabs are stored, then reduce-added, and
+    grad_c's MN-major operand falls back to 2-D boxes in the last chunk.  fp16
+    with an fp32 bias, 10% ignored rows, reduction 'sum'.  Against the float64
+    oracle: the loss over all rows, dE on sampled rows, dC and dBias on
+    sampled vocabulary rows (both ends of every chunk)."""
+    monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "16384")
     e, c, t, b = small(4200, 128, 36000, torch.float16, seed=11, bias=torch.float32, ignore=0.1)
     got = run(e, c, t, bias=b, reduction="sum")
     en, cn, bn = e.numpy(), c.numpy(), b.numpy()

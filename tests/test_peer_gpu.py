@@ -83,7 +83,8 @@ def raw_backward(e, c, t, peer_group=None, grad_e_f32=False):
     (300, 96, 3000, torch.float16),        # fp16 (scaled dlogits)
     (200, 100, 2000, torch.float32),       # CUDA-core path: push kernel
 ])
-def test_group_of_one_matches_oracle_and_plain_backward(N, D, V, dtype):
+def test_group_of_one_matches_oracle_and_plain_backward(N, D, V, dtype, monkeypatch):
+    monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "16384")   # N = 8300, V = 20000: two chunks
     e, c, t = inputs(N, D, V, dtype, seed=N + V)
     out_dtype = dtype
     buf = Buffer(_ext.lib.cce_peer_buffer_bytes(N, D, 1, _ext.dtype_code(out_dtype, "t")))
