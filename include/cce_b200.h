@@ -227,6 +227,39 @@ CCE_API int cce_dequantize(const uint32_t* wq, const void* scales, const void* b
                            void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Quantised classifier.  No counterpart in the reference's library: its
+ * mlx-lm recipe (README.md:84-95) dequantises the whole [V, D] head with MLX
+ * before every call.  Here the head stays quantised in HBM and the forward /
+ * backward expand one vocabulary chunk at a time into a workspace buffer (two
+ * buffers: the next chunk is expanded on a side stream while the current
+ * chunk's GEMMs run), in e's dtype.  The head is frozen: no gradient for it.
+ * --------------------------------------------------------------------------- */
+
+typedef struct CceQuantHead {
+  const uint32_t* wq;      /* [V][D * bits / 32] words, MLX's affine layout (see cce_dequantize) */
+  const void* scales;      /* [V][D / group_size] in scale_dtype                                 */
+  const void* biases;      /* [V][D / group_size] in scale_dtype                                 */
+  int32_t scale_dtype;     /* CCE_F32 / F16 / BF16                                               */
+  int32_t group_size;      /* 32, 64 or 128 (D must be a multiple)                               */
+  int32_t bits;            /* 2, 4 or 8                                                          */
+} CceQuantHead;
+
+/* cce_forward with the classifier given as a quantised head (V rows). */
+CCE_API size_t cce_forward_q_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype);
+CCE_API int cce_forward_q(const void* e, const CceQuantHead* head, const void* bias, int bias_dtype,
+                          const int32_t* targets, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                          int dtype, float* tile_max, float* lse, float* tgt, void* workspace,
+                          size_t workspace_bytes, void* stream);
+/* cce_backward with a quantised head: CCE_NEED_DE and / or CCE_NEED_DBIAS
+ * (CCE_NEED_DC is refused: the head is frozen). */
+CCE_API size_t cce_backward_q_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags);
+CCE_API int cce_backward_q(const void* e, const CceQuantHead* head, const void* bias, int bias_dtype,
+                           const int32_t* targets, const float* lse, const float* d_nll,
+                           const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
+                           int dtype, int flags, float filter_log_eps, void* grad_e, float* grad_bias,
+                           int64_t* skip_stats, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Vocabulary-sharded backward over NVLink peer memory.  No counterpart in the
  * reference (it has no multi-device code); this is the cross-rank sum of
  * grad_e that the sharded path needs, done with the ranks' own loads and

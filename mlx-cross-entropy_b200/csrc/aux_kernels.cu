@@ -85,17 +85,20 @@ lse_combine_kernel(const float* __restrict__ part_max, const float* __restrict__
   }
 }
 
-// One block = one 128-row block x kMaskTiles statistics tiles; each warp
-// decides kMaskTiles / 8 tiles, its lane l covering rows l, l + 32, l + 64 and
-// l + 96 (coalesced tile_max loads, per-row inputs read once).  Besides the
-// byte mask keep[row block][tile], the block ORs its decisions per 128-column
-// tile into the transposed bit table keep_t[128-column tile][row block bits]
-// (zeroed by the caller; nullable).  The skip counters take one atomic pair
-// per block.
+// One block = one 128-row block x kMaskRounds x kMaskTiles statistics tiles;
+// in each round every warp decides kMaskTiles / 8 tiles, its lane l covering
+// rows l, l + 32, l + 64 and l + 96 (coalesced tile_max loads, per-row inputs
+// read once per block).  Besides the byte mask keep[row block][tile], the
+// block ORs its decisions per 128-column tile into the transposed bit table
+// keep_t[128-column tile][row block bits] (zeroed by the caller; nullable).
+// The skip counters take one atomic pair per block: blocks span 256 tiles so
+// that there are few of them (at 32 tiles per block the ~4000 blocks of
+// config 3 serialised on the two counter addresses).
 constexpr int kMaskTiles = 32;
+constexpr int kMaskRounds = 8;
 constexpr int kMaskWarps = 8;
 constexpr int kTilesPer128 = 128 / kStatTile;
-static_assert(kMaskTiles % kTilesPer128 == 0, "whole 128-column tiles per block");
+static_assert(kMaskTiles % kTilesPer128 == 0, "whole 128-column tiles per round");
 
 __global__ void __launch_bounds__(kMaskWarps * 32)
 block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ lse,
@@ -103,8 +106,11 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
                   int64_t V, int64_t v_offset, float log_eps, int no_filter, uint8_t* __restrict__ keep,
                   uint32_t* __restrict__ keep_t, int64_t keep_t_ld,
                   unsigned long long* __restrict__ skip_stats) {
-  __shared__ uint32_t any128[kMaskTiles / kTilesPer128];
-  if (threadIdx.x < kMaskTiles / kTilesPer128) any128[threadIdx.x] = 0;
+  constexpr int kGroups = kMaskRounds * kMaskTiles / kTilesPer128;  // 128-column tiles per block
+  __shared__ uint32_t any128[kGroups];
+  __shared__ int cnt[2];
+  if (threadIdx.x < kGroups) any128[threadIdx.x] = 0;
+  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0;
   __syncthreads();
   const int64_t nVt = ceil_div(V, kStatTile);
   const int64_t i = blockIdx.y;  // row block
@@ -122,50 +128,53 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
     tl[u] = live[u] ? (int64_t)targets[row] - v_offset : -1;
     tm[u] = tile_max + (live[u] ? row : 0);
   }
-  // all of this warp's tile maxima are loaded before any is tested, so the
-  // loads overlap
   constexpr int kTilesPerWarp = kMaskTiles / kMaskWarps;
-  float x[kTilesPerWarp][kRowsPerLane];
-#pragma unroll
-  for (int q = 0; q < kTilesPerWarp; ++q) {
-    const int64_t j = (int64_t)blockIdx.x * kMaskTiles + warp + q * kMaskWarps;
-#pragma unroll
-    for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = (live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
-  }
   int skipped = 0, total = 0;
+  const int64_t tile0 = (int64_t)blockIdx.x * kMaskRounds * kMaskTiles;
+#pragma unroll 1
+  for (int r = 0; r < kMaskRounds; ++r) {
+    const int64_t base = tile0 + (int64_t)r * kMaskTiles;
+    if (base >= nVt) break;
+    // all of this warp's tile maxima of the round are loaded before any is
+    // tested, so the loads overlap
+    float x[kTilesPerWarp][kRowsPerLane];
 #pragma unroll
-  for (int q = 0; q < kTilesPerWarp; ++q) {
-    const int w = warp + q * kMaskWarps;
-    const int64_t j = (int64_t)blockIdx.x * kMaskTiles + w;  // vocabulary tile
-    if (j >= nVt) break;
-    bool k = false;
+    for (int q = 0; q < kTilesPerWarp; ++q) {
+      const int64_t j = base + warp + q * kMaskWarps;
 #pragma unroll
-    for (int u = 0; u < kRowsPerLane; ++u) {
-      if (live[u]) {
-        const bool hit = tl[u] >= j * kStatTile && tl[u] < (j + 1) * kStatTile && tl[u] < V;
-        k = k || no_filter || hit || (x[q][u] - L[u] >= log_eps);
+      for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = (live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
+    }
+#pragma unroll
+    for (int q = 0; q < kTilesPerWarp; ++q) {
+      const int w = warp + q * kMaskWarps;
+      const int64_t j = base + w;  // vocabulary tile
+      if (j >= nVt) break;
+      bool k = false;
+#pragma unroll
+      for (int u = 0; u < kRowsPerLane; ++u) {
+        if (live[u]) {
+          const bool hit = tl[u] >= j * kStatTile && tl[u] < (j + 1) * kStatTile && tl[u] < V;
+          k = k || no_filter || hit || (x[q][u] - L[u] >= log_eps);
+        }
       }
+      k = __any_sync(0xffffffffu, k);
+      if (lane == 0) {
+        keep[i * nVt + j] = (uint8_t)k;
+        if (k) any128[(r * kMaskTiles + w) / kTilesPer128] = 1u;  // benign race: every writer stores 1
+      }
+      ++total;
+      skipped += k ? 0 : 1;
     }
-    k = __any_sync(0xffffffffu, k);
-    if (lane == 0) {
-      keep[i * nVt + j] = (uint8_t)k;
-      if (k) any128[w / kTilesPer128] = 1u;  // benign race: every writer stores 1
-    }
-    ++total;
-    skipped += k ? 0 : 1;
   }
-  __shared__ int cnt[2];
-  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0;
-  __syncthreads();
   if (skip_stats && lane == 0 && total) {
     atomicAdd(&cnt[0], skipped);
     atomicAdd(&cnt[1], total);
   }
-  if (keep_t && threadIdx.x < kMaskTiles / kTilesPer128 && any128[threadIdx.x]) {
-    const int64_t m = (int64_t)blockIdx.x * (kMaskTiles / kTilesPer128) + threadIdx.x;  // 128-column tile
+  __syncthreads();
+  if (keep_t && threadIdx.x < kGroups && any128[threadIdx.x]) {
+    const int64_t m = tile0 / kTilesPer128 + threadIdx.x;  // 128-column tile
     atomicOr(&keep_t[m * keep_t_ld + (i >> 5)], 1u << (i & 31));
   }
-  __syncthreads();
   if (skip_stats && threadIdx.x == 0 && cnt[1]) {
     atomicAdd(&skip_stats[0], (unsigned long long)cnt[0]);
     atomicAdd(&skip_stats[1], (unsigned long long)cnt[1]);
@@ -258,7 +267,8 @@ cudaError_t launch_block_mask(const float* tile_max, const float* lse, const int
                               float log_eps, bool no_filter, uint8_t* keep, uint32_t* keep_t,
                               int64_t keep_t_ld, int64_t* skip_stats, cudaStream_t stream) {
   if (N == 0 || V == 0) return cudaSuccess;
-  dim3 grid((unsigned)ceil_div(ceil_div(V, kStatTile), (int64_t)kMaskTiles), (unsigned)ceil_div(N, kRowBlock));
+  dim3 grid((unsigned)ceil_div(ceil_div(V, kStatTile), (int64_t)(kMaskTiles * kMaskRounds)),
+            (unsigned)ceil_div(N, kRowBlock));
   block_mask_kernel<<<grid, kMaskWarps * 32, 0, stream>>>(tile_max, lse, targets, d_nll, N, V, v_offset,
                                                     log_eps, no_filter ? 1 : 0, keep, keep_t, keep_t_ld,
                                                     reinterpret_cast<unsigned long long*>(skip_stats));

@@ -79,17 +79,20 @@ int cuda_fail(cudaError_t err, const char* where) {
   } while (0)
 
 constexpr size_t kAlign = 256;
-// dlogits chunk buffer: aim for 32768 vocabulary rows per chunk, within 1 GiB,
-// and never below 512 MiB.  Every chunk costs three kernel launches whatever
-// its work (~70 us at N = 2048 when the filter rejects nearly every block), so
-// small N gets long chunks: measured on B200, config 4 (N = 2048) backward
-// 1.44 ms in 8 chunks -> 1.01 ms in 2, config 2 (N = 1024) 0.65 -> 0.52 ms in
-// one; config 3 (N = 4096) 8.71 ms at 16384 rows, 8.35 at 32768, 8.42 at
-// 65536, 8.62 at 131072.  (Two buffers, so that a chunk's dlogits overlap the
-// previous chunk's grads, measured no faster.)
+// dlogits chunk buffer: aim for 32768 vocabulary rows per chunk within 128 MiB
+// to 1 GiB of buffer.  Every chunk costs three kernel launches whatever its
+// work (~70 us at N = 2048 when the filter rejects nearly every block), so
+// smaller N may grow its chunks up to 256 MiB of buffer, but never past half
+// of the vocabulary: the buffer stays below half of the [N, V] logits, the
+// memory bound of the whole method.  Measured on B200: config 3 (N = 4096)
+// backward 8.71 ms at 16384 rows, 8.35 at 32768, 8.42 at 65536, 8.62 at
+// 131072; config 4 (N = 2048) 1.44 ms in 8 chunks, 1.15 in 4, 1.01 in 2;
+// config 2 (N = 1024) 0.65 ms in 2 chunks.  (Two buffers, so that a chunk's
+// dlogits overlap the previous chunk's grads, measured no faster.)
 constexpr int64_t kDlTargetRows = 32768;
 constexpr int64_t kDlMaxBytes = 1ll << 30;
-constexpr int64_t kDlMinBytes = 512ll << 20;
+constexpr int64_t kDlMinBytes = 128ll << 20;
+constexpr int64_t kDlSmallNBytes = 256ll << 20;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -152,6 +155,13 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   if (budget < kDlMinBytes && target == kDlTargetRows) budget = kDlMinBytes;
   int64_t vc = (budget / (nrow * elt)) / gran * gran;
   if (vc < gran) vc = gran;
+  if (target == kDlTargetRows && nrow * elt * target < kDlSmallNBytes) {
+    // small N: longer chunks, up to 256 MiB and half the vocabulary
+    const int64_t half = cce::round_up(cce::ceil_div(V > 0 ? V : 1, 2), gran);
+    int64_t grow = (kDlSmallNBytes / (nrow * elt)) / gran * gran;
+    if (grow > half) grow = half;
+    if (grow > vc) vc = grow;
+  }
   const int64_t vmax = cce::round_up(V > 0 ? V : 1, gran);
   if (vc > vmax) vc = vmax;
   p.vc = vc;
@@ -206,7 +216,10 @@ int check_sizes(int64_t N, int64_t D, int64_t V, int dtype) {
 struct SideStreams {
   unsigned long long ctx_id = 0;
   cudaStream_t se = nullptr, sc = nullptr;
+  cudaStream_t sq = nullptr;  // dequantisation of a quantised head's next chunk
   cudaEvent_t start = nullptr, ev_l = nullptr, ev_e = nullptr, ev_c = nullptr;
+  cudaEvent_t ev_q[2] = {nullptr, nullptr};  // chunk buffer b holds its dequantised chunk
+  cudaEvent_t ev_r = nullptr;                // the other chunk buffer's readers are done
 };
 
 thread_local SideStreams g_side[64];
@@ -226,10 +239,14 @@ int side_streams(SideStreams** out) {
     SideStreams n;
     if ((err = cudaStreamCreateWithPriority(&n.se, cudaStreamNonBlocking, hi)) != cudaSuccess ||
         (err = cudaStreamCreateWithPriority(&n.sc, cudaStreamNonBlocking, lo)) != cudaSuccess ||
+        (err = cudaStreamCreateWithPriority(&n.sq, cudaStreamNonBlocking, lo)) != cudaSuccess ||
         (err = cudaEventCreateWithFlags(&n.start, cudaEventDisableTiming)) != cudaSuccess ||
         (err = cudaEventCreateWithFlags(&n.ev_l, cudaEventDisableTiming)) != cudaSuccess ||
         (err = cudaEventCreateWithFlags(&n.ev_e, cudaEventDisableTiming)) != cudaSuccess ||
-        (err = cudaEventCreateWithFlags(&n.ev_c, cudaEventDisableTiming)) != cudaSuccess)
+        (err = cudaEventCreateWithFlags(&n.ev_c, cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_q[0], cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_q[1], cudaEventDisableTiming)) != cudaSuccess ||
+        (err = cudaEventCreateWithFlags(&n.ev_r, cudaEventDisableTiming)) != cudaSuccess)
       return cuda_fail(err, "creating the backward side streams");
     // creating them made a context current if none was
     if (!cce::current_context_id(&n.ctx_id)) return fail(CCE_ERR_CUDA, "could not read the current CUDA context");
@@ -418,6 +435,46 @@ int cce_selftest_wait_timeout(int64_t limit_ns, void* stream) {
 
 int64_t cce_num_stat_tiles(int64_t V) { return V <= 0 ? 0 : cce::ceil_div(V, cce::kStatTile); }
 
+// A quantised head's arguments are usable for rows of width D.
+static int check_head(const CceQuantHead* h, int64_t D, const char* what) {
+  if (!h || !h->wq || !h->scales || !h->biases) return fail(CCE_ERR_ARG, "%s: NULL quantised-head pointer", what);
+  if (h->bits != 2 && h->bits != 4 && h->bits != 8)
+    return fail(CCE_ERR_ARG, "%s: bits must be 2, 4 or 8, got %d", what, h->bits);
+  if (h->group_size != 32 && h->group_size != 64 && h->group_size != 128)
+    return fail(CCE_ERR_ARG, "%s: group_size must be 32, 64 or 128, got %d", what, h->group_size);
+  if (D % h->group_size != 0)
+    return fail(CCE_ERR_SHAPE, "%s: D=%lld is not a multiple of group_size=%d", what, (long long)D, h->group_size);
+  if (!dtype_ok(h->scale_dtype)) return fail(CCE_ERR_DTYPE, "%s: scale dtype code %d", what, h->scale_dtype);
+  return CCE_OK;
+}
+
+// Rows [v0, v0 + rows) of a quantised head expanded into `out` (dtype), on `s`.
+static cudaError_t dequant_rows(const CceQuantHead* h, int64_t v0, int64_t rows, int64_t D, int dtype, void* out,
+                         cudaStream_t s) {
+  const int64_t wpr = D * h->bits / 32;
+  const int64_t gpr = D / h->group_size;
+  const size_t ssz = dtype_size(h->scale_dtype);
+  return cce::launch_dequantize(h->wq + v0 * wpr, static_cast<const char*>(h->scales) + v0 * gpr * ssz,
+                                static_cast<const char*>(h->biases) + v0 * gpr * ssz, h->scale_dtype, rows, D,
+                                h->group_size, h->bits, dtype, out, s);
+}
+
+// Bytes of one chunk buffer of a quantised head's expanded rows.
+static size_t chunk_buf_bytes(const BwdPlan& p, int64_t D, int dtype) {
+  return align_up((size_t)p.vc * (size_t)D * dtype_size(dtype));
+}
+
+static size_t backward_ws_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool quant) {
+  const BwdPlan ps = plan_backward(N, D, V, dtype, flags, false);
+  size_t b = plan_bytes(ps) + (quant ? 2 * chunk_buf_bytes(ps, D, dtype) : 0);
+  if (tc_candidate(dtype, D)) {
+    const BwdPlan pt = plan_backward(N, D, V, dtype, flags, true);
+    const size_t t = plan_bytes(pt) + (quant ? 2 * chunk_buf_bytes(pt, D, dtype) : 0);
+    if (t > b) b = t;
+  }
+  return b;
+}
+
 // The LSE partials (max, sum-exp) per row per kernel tile: 2 x ceil(V / 128) x N
 // floats covers both kernel families (tensor-core tiles are 256 columns wide).
 size_t cce_forward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
@@ -461,6 +518,82 @@ int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
   return CCE_OK;
 }
 
+// Rows of a quantised head expanded per forward chunk (two buffers).
+constexpr int64_t kFwdQuantChunkRows = 16384;
+
+static size_t forward_q_ws_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
+  const int64_t rows = V < kFwdQuantChunkRows ? (V > 0 ? V : 1) : kFwdQuantChunkRows;
+  return cce_forward_workspace_bytes(N, D, V, dtype) + 2 * align_up((size_t)rows * (size_t)D * dtype_size(dtype));
+}
+
+size_t cce_forward_q_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
+  return forward_q_ws_bytes(N, D, V, dtype);
+}
+
+int cce_forward_q(const void* e, const CceQuantHead* head, const void* bias, int bias_dtype,
+                  const int32_t* targets, int64_t N, int64_t D, int64_t V, int64_t v_offset, int dtype,
+                  float* tile_max, float* lse, float* tgt, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_sizes(N, D, V, dtype);
+  if (rc) return rc;
+  rc = check_head(head, D, "cce_forward_q");
+  if (rc) return rc;
+  if (bias && !dtype_ok(bias_dtype)) return fail(CCE_ERR_DTYPE, "unsupported bias dtype code %d", bias_dtype);
+  if (N == 0) return CCE_OK;
+  if (V == 0) return fail(CCE_ERR_SHAPE, "V must be positive");
+  if (!e || !targets || !tile_max || !lse || !tgt) return fail(CCE_ERR_ARG, "cce_forward_q: NULL required pointer");
+  const size_t need = forward_q_ws_bytes(N, D, V, dtype);
+  if (!workspace || workspace_bytes < need)
+    return fail(CCE_ERR_WORKSPACE, "cce_forward_q: workspace %zu bytes < required %zu", workspace_bytes, need);
+  rc = check_arch();
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t part_bytes = cce_forward_workspace_bytes(N, D, V, dtype);
+  char* cbuf[2] = {(char*)workspace + part_bytes, nullptr};
+  const int64_t vq = V < kFwdQuantChunkRows ? V : kFwdQuantChunkRows;
+  cbuf[1] = cbuf[0] + align_up((size_t)vq * (size_t)D * dtype_size(dtype));
+  const bool tc = !force_simt() && cce::tc_supported(e, cbuf[0], D, dtype);
+  const int64_t ptile = tc ? cce::kTcLseTile : cce::kSimtLseTile;
+  const int64_t P = cce::ceil_div(V, ptile);
+  float* part_m = (float*)workspace;
+  float* part_s = part_m + P * N;
+  SideStreams* ss = nullptr;
+  rc = side_streams(&ss);
+  if (rc) return rc;
+  CCE_CUDA_CHECK(cudaMemsetAsync(tgt, 0, (size_t)N * sizeof(float), s), "cce_forward_q memset");
+  CCE_CUDA_CHECK(cudaEventRecord(ss->start, s), "cce_forward_q fork");
+  CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sq, ss->start, 0), "cce_forward_q fork");
+  CCE_CUDA_CHECK(dequant_rows(head, 0, vq, D, dtype, cbuf[0], ss->sq), "cce_forward_q dequantise");
+  CCE_CUDA_CHECK(cudaEventRecord(ss->ev_q[0], ss->sq), "cce_forward_q record");
+  const int64_t nchunks = cce::ceil_div(V, vq);
+  const size_t bsz = bias ? dtype_size(bias_dtype) : 0;
+  for (int64_t k = 0; k < nchunks; ++k) {
+    const int64_t v0 = k * vq;
+    const int64_t rows = (V - v0) < vq ? (V - v0) : vq;
+    if (k + 1 < nchunks) {
+      // the buffer chunk k+1 goes into was read by forward(k-1), enqueued on `s` already
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_r, s), "cce_forward_q record");
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sq, ss->ev_r, 0), "cce_forward_q wait");
+      const int64_t v1 = v0 + vq;
+      const int64_t rows1 = (V - v1) < vq ? (V - v1) : vq;
+      CCE_CUDA_CHECK(dequant_rows(head, v1, rows1, D, dtype, cbuf[(k + 1) & 1], ss->sq), "cce_forward_q dequantise");
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_q[(k + 1) & 1], ss->sq), "cce_forward_q record");
+    }
+    CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_q[k & 1], 0), "cce_forward_q wait");
+    // this chunk's columns of the statistics and partials (vq is a multiple of both tile widths)
+    cce::FwdArgs a{e, cbuf[k & 1], bias ? static_cast<const char*>(bias) + v0 * bsz : nullptr, bias_dtype, targets,
+                   N, D, rows, v_offset + v0, dtype, tile_max + (v0 / cce::kStatTile) * N,
+                   part_m + (v0 / ptile) * N, part_s + (v0 / ptile) * N, tgt};
+    if (tc) {
+      CCE_CUDA_CHECK(cce::tc_forward(a, s), "cce_forward_q tc kernel");
+    } else {
+      CCE_CUDA_CHECK(cce::simt_forward(a, s), "cce_forward_q simt kernel");
+    }
+  }
+  CCE_CUDA_CHECK(cce::launch_lse_combine(part_m, part_s, nullptr, P, N, N, lse, nullptr, nullptr, s),
+                 "cce_forward_q combine");
+  return CCE_OK;
+}
+
 int cce_lse_combine(const float* part_lse, const float* part_tgt, int64_t P, int64_t N,
                     int64_t part_stride, float* lse, float* tgt, float* nll, void* stream) {
   if (P <= 0 || N < 0) return fail(CCE_ERR_SHAPE, "cce_lse_combine: bad P=%lld N=%lld", (long long)P, (long long)N);
@@ -479,17 +612,14 @@ int cce_lse_combine(const float* part_lse, const float* part_tgt, int64_t P, int
 }
 
 size_t cce_backward_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags) {
-  size_t b = plan_bytes(plan_backward(N, D, V, dtype, flags, false));
-  if (tc_candidate(dtype, D)) {
-    const size_t t = plan_bytes(plan_backward(N, D, V, dtype, flags, true));
-    if (t > b) b = t;
-  }
-  return b;
+  return backward_ws_bytes(N, D, V, dtype, flags, false);
 }
 
-// cce_backward, and cce_backward_peer when `pg` is given (grad_e summed over
-// the group through the exchange buffers).
-static int backward_impl(const void* e, const void* c, const void* bias, int bias_dtype,
+// cce_backward, cce_backward_peer when `pg` is given (grad_e summed over the
+// group through the exchange buffers), and cce_backward_q when `qh` is given
+// (c is a quantised head: every vocabulary chunk is expanded into one of two
+// workspace buffers on a side stream while the previous chunk's GEMMs run).
+static int backward_impl(const void* e, const void* c, const CceQuantHead* qh, const void* bias, int bias_dtype,
                          const int32_t* targets, const float* lse, const float* d_nll,
                          const float* tile_max, int64_t N, int64_t D, int64_t V, int64_t v_offset,
                          int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
@@ -502,6 +632,11 @@ static int backward_impl(const void* e, const void* c, const void* bias, int bia
     return fail(CCE_ERR_ARG, "cce_backward: unknown flag bits 0x%x", flags);
   const bool need_de = flags & CCE_NEED_DE, need_dc = flags & CCE_NEED_DC,
              need_db = flags & CCE_NEED_DBIAS;
+  if (qh) {
+    rc = check_head(qh, D, "cce_backward_q");
+    if (rc) return rc;
+    if (need_dc) return fail(CCE_ERR_ARG, "cce_backward_q: a quantised head is frozen (no CCE_NEED_DC)");
+  }
   // A zero-size output may come with a NULL pointer (torch gives empty tensors none).
   if ((need_de && N > 0 && !grad_e) || (need_dc && V > 0 && !grad_c) || (need_db && V > 0 && !grad_bias))
     return fail(CCE_ERR_ARG, "cce_backward: a requested gradient has a NULL output pointer");
@@ -517,12 +652,13 @@ static int backward_impl(const void* e, const void* c, const void* bias, int bia
     if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
     return CCE_OK;
   }
-  if (!e || !c || !targets || !lse || !d_nll || !tile_max)
+  if (!e || (!c && !qh) || !targets || !lse || !d_nll || !tile_max)
     return fail(CCE_ERR_ARG, "cce_backward: NULL required pointer");
-  const bool tc = !force_simt() && cce::tc_backward_supported(e, c, D, dtype) && aligned16(workspace) &&
-                  (!need_de || aligned16(grad_e)) && (!need_dc || aligned16(grad_c));
+  // (a quantised head's chunks live in the workspace: its alignment stands for c's)
+  const bool tc = !force_simt() && cce::tc_backward_supported(e, qh ? workspace : c, D, dtype) &&
+                  aligned16(workspace) && (!need_de || aligned16(grad_e)) && (!need_dc || aligned16(grad_c));
   const BwdPlan p = plan_backward(N, D, V, dtype, flags, tc);
-  const size_t need = cce_backward_workspace_bytes(N, D, V, dtype, flags);
+  const size_t need = backward_ws_bytes(N, D, V, dtype, flags, qh != nullptr);
   if (!workspace || workspace_bytes < need)
     return fail(CCE_ERR_WORKSPACE, "cce_backward: workspace %zu bytes < required %zu", workspace_bytes, need);
 
@@ -554,6 +690,11 @@ static int backward_impl(const void* e, const void* c, const void* bias, int bia
   uint32_t* keep_t = p.keep_t_bytes
                          ? (uint32_t*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes)
                          : nullptr;
+  char* cbuf[2] = {nullptr, nullptr};  // a quantised head's expanded chunks
+  if (qh) {
+    cbuf[0] = ws + plan_bytes(p);
+    cbuf[1] = cbuf[0] + chunk_buf_bytes(p, D, dtype);
+  }
   if (p.tc) CCE_CUDA_CHECK(cudaMemsetAsync(counters, 0, p.counter_bytes, s), "cce_backward memset counters");
   if (keep_t) CCE_CUDA_CHECK(cudaMemsetAsync(keep_t, 0, p.keep_t_bytes, s), "cce_backward memset mask table");
   if (scale) CCE_CUDA_CHECK(cce::launch_pow2_absmax(d_nll, N, scale, s), "cce_backward scale");
@@ -563,29 +704,54 @@ static int backward_impl(const void* e, const void* c, const void* bias, int bia
                  "cce_backward mask");
   if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
 
-  cce::BwdChunkArgs a{e, c, bias, bias_dtype, targets, lse, d_nll, keep, keep_t, p.keep_t_ld, N, D, V, v_offset, dtype,
-                      0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr, scale};
+  cce::BwdChunkArgs a{e, c, nullptr, bias, bias_dtype, targets, lse, d_nll, keep, keep_t, p.keep_t_ld, N, D, V,
+                      v_offset, dtype, 0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr, scale};
   const int64_t nchunks = cce::ceil_div(V, p.vc);
+  const size_t esz = dtype_size(dtype);
   SideStreams* ss = nullptr;
-  if (p.tc) {
+  if (p.tc || qh) {
     rc = side_streams(&ss);
     if (rc) return rc;
     // fork: the side streams start after everything enqueued on `s` so far
     CCE_CUDA_CHECK(cudaEventRecord(ss->start, s), "cce_backward fork");
-    CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->start, 0), "cce_backward fork");
-    CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->start, 0), "cce_backward fork");
+    if (p.tc) {
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->start, 0), "cce_backward fork");
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sc, ss->start, 0), "cce_backward fork");
+    }
+    if (qh) {
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sq, ss->start, 0), "cce_backward fork");
+      const int64_t rows0 = V < p.vc ? V : p.vc;
+      CCE_CUDA_CHECK(dequant_rows(qh, 0, rows0, D, dtype, cbuf[0], ss->sq), "cce_backward_q dequantise");
+      CCE_CUDA_CHECK(cudaEventRecord(ss->ev_q[0], ss->sq), "cce_backward record");
+    }
   }
   for (int64_t ch = 0; ch < nchunks; ++ch) {
     a.vc0 = ch * p.vc;
     a.vc_len = (V - a.vc0) < p.vc ? (V - a.vc0) : p.vc;
     const bool last = ch == nchunks - 1;
     a.counters = counters + 3 * ch;
-    if (p.tc) {
-      // dlogits(ch) on `s` overwrites the buffer grad_e / grad_c of chunk ch-1 read
-      if (ch > 0) {
-        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_e, 0), "cce_backward join");
-        CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_c, 0), "cce_backward join");
+    // dlogits(ch) on `s` overwrites the buffer grad_e / grad_c of chunk ch-1 read
+    if (p.tc && ch > 0) {
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_e, 0), "cce_backward join");
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_c, 0), "cce_backward join");
+    }
+    if (qh) {
+      // chunk ch+1 goes into the buffer chunk ch-1 was read from (all of
+      // whose readers `s` has now waited for); chunk ch was expanded already
+      if (!last) {
+        CCE_CUDA_CHECK(cudaEventRecord(ss->ev_r, s), "cce_backward record");
+        CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->sq, ss->ev_r, 0), "cce_backward wait");
+        const int64_t v1 = a.vc0 + p.vc;
+        const int64_t rows1 = (V - v1) < p.vc ? (V - v1) : p.vc;
+        CCE_CUDA_CHECK(dequant_rows(qh, v1, rows1, D, dtype, cbuf[(ch + 1) & 1], ss->sq), "cce_backward_q dequantise");
+        CCE_CUDA_CHECK(cudaEventRecord(ss->ev_q[(ch + 1) & 1], ss->sq), "cce_backward record");
       }
+      CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_q[ch & 1], 0), "cce_backward wait");
+      a.c_chunk = cbuf[ch & 1];
+    } else {
+      a.c_chunk = static_cast<const char*>(c) + (size_t)a.vc0 * (size_t)D * esz;
+    }
+    if (p.tc) {
       CCE_CUDA_CHECK(cce::tc_dlogits(a, s), "cce_backward tc dlogits");
       CCE_CUDA_CHECK(cudaEventRecord(ss->ev_l, s), "cce_backward record");
       CCE_CUDA_CHECK(cudaStreamWaitEvent(ss->se, ss->ev_l, 0), "cce_backward wait");
@@ -630,9 +796,9 @@ int cce_backward(const void* e, const void* c, const void* bias, int bias_dtype,
                  int dtype, int flags, float filter_log_eps, void* grad_e, void* grad_c,
                  float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes,
                  void* stream) {
-  return backward_impl(e, c, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype, flags,
-                       filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes, nullptr,
-                       stream);
+  return backward_impl(e, c, nullptr, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype,
+                       flags, filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes,
+                       nullptr, stream);
 }
 
 int cce_backward_peer(const void* e, const void* c, const void* bias, int bias_dtype,
@@ -648,9 +814,23 @@ int cce_backward_peer(const void* e, const void* c, const void* bias, int bias_d
   for (int r = 0; r < group->world; ++r)
     if (!group->bases[r] || !aligned16(group->bases[r]))
       return fail(CCE_ERR_ARG, "cce_backward_peer: buffer of rank %d is NULL or not 16-byte aligned", r);
-  return backward_impl(e, c, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype, flags,
-                       filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes, group,
+  return backward_impl(e, c, nullptr, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype,
+                       flags, filter_log_eps, grad_e, grad_c, grad_bias, skip_stats, workspace, workspace_bytes, group,
                        stream);
+}
+
+size_t cce_backward_q_workspace_bytes(int64_t N, int64_t D, int64_t V, int dtype, int flags) {
+  return backward_ws_bytes(N, D, V, dtype, flags, true);
+}
+
+int cce_backward_q(const void* e, const CceQuantHead* head, const void* bias, int bias_dtype,
+                   const int32_t* targets, const float* lse, const float* d_nll, const float* tile_max, int64_t N,
+                   int64_t D, int64_t V, int64_t v_offset, int dtype, int flags, float filter_log_eps, void* grad_e,
+                   float* grad_bias, int64_t* skip_stats, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!head) return fail(CCE_ERR_ARG, "cce_backward_q: NULL head");
+  return backward_impl(e, nullptr, head, bias, bias_dtype, targets, lse, d_nll, tile_max, N, D, V, v_offset, dtype,
+                       flags, filter_log_eps, grad_e, nullptr, grad_bias, skip_stats, workspace, workspace_bytes,
+                       nullptr, stream);
 }
 
 size_t cce_peer_buffer_bytes(int64_t N, int64_t D, int world, int out_dtype) {

@@ -37,7 +37,9 @@ struct FwdArgs {
 
 struct BwdChunkArgs {
   const void* e;
-  const void* c;
+  const void* c;         // row 0 of this call's c (the dense head; nullptr for a quantised one)
+  const void* c_chunk;   // row vc0 of c: the chunk's vc_len rows (the dequantised chunk buffer
+                         // for a quantised head); the chunk kernels read c through it
   const void* bias;
   int bias_dtype;
   const int32_t* targets;

@@ -179,7 +179,8 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
     return;
   }
   float acc[4][8];
-  tile_logits<T>(e, c, N, D, V, r0, v0, acc);
+  // c holds the chunk's rows: row 0 = local vocab id vc0
+  tile_logits<T>(e, c, N, D, vend - vc0, r0, v0 - vc0, acc);
   __shared__ float colsum[BN];
   if (grad_bias) {
     for (int idx = threadIdx.x; idx < BN; idx += THREADS) colsum[idx] = 0.f;
@@ -319,7 +320,7 @@ template <typename T>
 cudaError_t dl_dispatch_bias(const BwdChunkArgs& a, cudaStream_t s) {
   dim3 grid((unsigned)ceil_div(a.N, BM), (unsigned)ceil_div(a.vc_len, BN));
   const T* e = (const T*)a.e;
-  const T* c = (const T*)a.c;
+  const T* c = (const T*)a.c_chunk;
   float* dl = (float*)a.dlogits;
 #define CCE_DL_LAUNCH(TB)                                                                        \
   simt_dlogits_kernel<T, TB><<<grid, THREADS, 0, s>>>(e, c, a.bias, a.targets, a.lse, a.d_nll,    \
@@ -359,12 +360,12 @@ cudaError_t simt_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
 
 cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, cudaStream_t s) {
   if (a.N == 0 || a.D == 0) return cudaSuccess;
-  // A(m = row, k = v) = dl[row * ld + v]; B(k = v, n = d) = c[(vc0 + v) * D + d]
+  // A(m = row, k = v) = dl[row * ld + v]; B(k = v, n = d) = c_chunk[v * D + d] (row vc0 + v of c)
   dim3 grid((unsigned)ceil_div(a.D, GN), (unsigned)ceil_div(a.N, GM));
   const float* dl = (const float*)a.dlogits;
 #define CCE_GE_LAUNCH(T)                                                                       \
   simt_gemm_kernel<T, float, false><<<grid, THREADS, 0, s>>>(                                  \
-      dl, a.vc_ld, 1, (const T*)a.c + a.vc0 * a.D, a.D, 1, a.N, a.D, a.vc_len, grad_e_acc, a.D, \
+      dl, a.vc_ld, 1, (const T*)a.c_chunk, a.D, 1, a.N, a.D, a.vc_len, grad_e_acc, a.D, \
       accumulate)
   switch (a.dtype) {
     case CCE_F32: CCE_GE_LAUNCH(float); break;

@@ -72,6 +72,11 @@ constexpr uint32_t SMASK_BYTES = 16384;   // shared copy of the chunk's filter-m
 constexpr uint32_t OUT_STAGE_BYTES = 4 * 4096;  // epilogue output staging, 4 KB per epilogue warp
 constexpr size_t SMEM_BYTES = 1024 + STAGES * (size_t)STAGE_BYTES + OUT_STAGE_BYTES + 256 + SMASK_BYTES;
 constexpr int kPushWaitCode = 8;  // status code: a push unit's epilogue threads never all arrived
+// K-major B loaded as 32-row boxes (B32_BYTES each) when a tile's live column
+// groups are one run of at most this many groups (kNarrowB epilogues): a box
+// costs on its own, so longer runs load the whole tile in one box.
+constexpr uint32_t kNarrowMaxGroups = 2;
+constexpr uint32_t B32_BYTES = kStatTile * BK * 2;  // 4 KB: 32 rows x 128 bytes
 
 // Executed tensor-core work per kernel kind (0 forward, 1 dlogits, 2 grad_e,
 // 3 grad_c): the sum of N over every issued M = 128, K = 16 MMA, added once
@@ -186,6 +191,7 @@ struct Stager {
 
 template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
+  static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr int kKind = 0;  // slot in g_mma_cols
   const int32_t* targets;
   const void* bias;
@@ -269,6 +275,7 @@ struct FwdEpi {
 
 template <typename T, typename TB>
 struct DlogitsEpi {
+  static constexpr bool kNarrowB = true;  // B rows loaded for a tile's live column run only
   static constexpr int kKind = 1;  // slot in g_mma_cols
   const int32_t* targets;
   const float* lse;
@@ -351,10 +358,11 @@ struct DlogitsEpi {
     // read; grad_e reads kept groups only.
     if ((st.kmask >> (kStatsPerM * (c >> 2))) & ((1u << kStatsPerM) - 1u))
       sg.store16<T>(v, (int)(cb - vc0), st.y0);
-    if (grad_bias != nullptr) {
+    // (kept is the same for the whole warp: a rejected group is all zeros)
+    if (grad_bias != nullptr && kept) {
       const int lane = threadIdx.x & 31;
       const float colsum = warp_transpose_sum32(v);
-      if (kept && cb + lane < vc_end && colsum != 0.f) atomicAdd(grad_bias + cb + lane, colsum * st.s);
+      if (cb + lane < vc_end && colsum != 0.f) atomicAdd(grad_bias + cb + lane, colsum * st.s);
     }
   }
 
@@ -378,6 +386,7 @@ struct DlogitsEpi {
 // 16-byte stores over NVLink while the MMAs of the next units run; the last
 // unit raises the `pushed` flag on every rank.  The slabs are not written.
 struct GradEEpi {
+  static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr int kKind = 2;  // slot in g_mma_cols
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
@@ -507,6 +516,7 @@ struct GradEEpi {
 
 template <typename T>
 struct GradCEpi {
+  static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr int kKind = 3;  // slot in g_mma_cols
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
@@ -621,8 +631,8 @@ __device__ __forceinline__ void load_mask_view(const Epi& epi, uint8_t* smask, M
 template <bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, const Sched sched, const Epi epi,
-               const uint32_t idesc) {
+               const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmC,
+               const Sched sched, const Epi epi, const uint32_t idesc) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -661,6 +671,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if constexpr (Epi::kNarrowB) prefetch_tmap(&tmB32);
   }
   // Filter-mask slice: copied to shared memory when it fits, else read in place.
   MaskView mk{nullptr, nullptr, 0, 0, 0};
@@ -694,10 +705,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         sched.coords(tile, mb, nb, ks);
         sched.krange(ks, kb0, kb1);
         if (!epi.tile_active(mk, mb, nb)) continue;
+        // B rows to load: the whole tile, or (K-major B, kNarrowB) only a
+        // short run of live 32-column groups [nj0, nj0 + nn0) -- the rows
+        // the MMA of this tile reads (see the MMA issuer)
+        uint32_t nj0 = 0, nn0 = kGroups;
+        if constexpr (Epi::kNarrowB && !B_MN) {
+          const uint32_t cm = epi.col_mask(mk, mb, nb);
+          if (cm != kAllGroups) {
+            const uint32_t j = __ffs(cm) - 1;
+            const uint32_t n = __ffs(~(cm >> j)) - 1;
+            if ((cm >> (j + n)) == 0u && n <= kNarrowMaxGroups) {
+              nj0 = j;
+              nn0 = n;
+            }
+          }
+        }
+        const uint32_t tx_bytes = A_BYTES + (nn0 < (uint32_t)kGroups ? nn0 * B32_BYTES : B_BYTES);
         bool ok = true;
         for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(full + stage, STAGE_BYTES);
+          mbar_arrive_expect_tx(full + stage, tx_bytes);
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
           const int k0 = kb * BK;
@@ -719,6 +746,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               for (int j = 0; j < BN / 64; ++j)
                 tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
             }
+          } else if (nn0 < (uint32_t)kGroups) {
+            for (uint32_t g = nj0; g < nj0 + nn0; ++g)
+              tma_load_2d(b + g * B32_BYTES, &tmB32, full + stage, k0, nb * BN + (int)(g * kStatTile));
           } else {
             tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
           }
@@ -1013,8 +1043,8 @@ cudaError_t ensure_smem_attr(K kern, size_t bytes, std::atomic<unsigned long lon
 }
 
 template <bool A_MN, bool B_MN, class Epi>
-cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
-                        const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB32,
+                        const CUtensorMap& tmC, const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<A_MN, B_MN, Epi>;
   static std::atomic<unsigned long long> attr_ctx[64];
   cudaError_t err = ensure_smem_attr(kern, SMEM_BYTES, attr_ctx);
@@ -1023,7 +1053,7 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmC, s, epi, idesc);
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmB32, tmC, s, epi, idesc);
   return launched();
 }
 
@@ -1055,14 +1085,14 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
            nullptr, raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.part_m, a.part_s, a.tgt, a.N, a.V, a.v_offset};
   const CUtensorMap tmC{};  // the forward epilogue writes no tiles
-  return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, false>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
 }
 
 template <typename T, typename TB>
 cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
   CUtensorMap tmA, tmB;
-  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  const void* cchunk = a.c_chunk;
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
   Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
@@ -1072,9 +1102,10 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                         a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
-  CUtensorMap tmC;
+  CUtensorMap tmC, tmB32;
   if (!make_tmap_out(&tmC, a.dlogits, a.dtype, a.vc_len, a.N, a.vc_ld)) return cudaErrorInvalidValue;
-  return launch_gemm<false, false>(tmA, tmB, tmC, sc, epi, bf16, s);
+  if (!make_tmap(&tmB32, cchunk, bf16, a.D, a.vc_len, a.D, BK, kStatTile)) return cudaErrorInvalidValue;
+  return launch_gemm<false, false>(tmA, tmB, tmB32, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace
@@ -1115,7 +1146,7 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
                           cudaStream_t s) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tmA, tmB, tmC;
-  const void* cchunk = static_cast<const uint16_t*>(a.c) + a.vc0 * a.D;
+  const void* cchunk = a.c_chunk;
   if (!make_tmap(&tmA, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK, BM)) return cudaErrorInvalidValue;
   int b3d = 0;
   if (!make_tmap_mn(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, (BN) / 64, &b3d))
@@ -1131,7 +1162,7 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
     epi.peers = push->peers;
     epi.layout = push->layout;
   }
-  return launch_gemm<false, true>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, true>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
 }
 
 template <typename T>
@@ -1150,7 +1181,7 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;
-  return launch_gemm<true, true>(tmA, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<true, true>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace

@@ -57,7 +57,14 @@ EXPORTED_SYMBOLS = (
     "cce_backward_workspace_bytes", "cce_backward", "cce_dequantize", "cce_selftest_wait_timeout",
     "cce_peer_buffer_bytes", "cce_peer_buffer_alloc", "cce_peer_buffer_open", "cce_peer_buffer_close",
     "cce_peer_buffer_free", "cce_backward_peer", "cce_mma_flops",
+    "cce_forward_q_workspace_bytes", "cce_forward_q", "cce_backward_q_workspace_bytes", "cce_backward_q",
 )
+
+
+class CceQuantHead(ctypes.Structure):
+    """Mirror of ``CceQuantHead`` (include/cce_b200.h)."""
+    _fields_ = [("wq", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("biases", ctypes.c_void_p),
+                ("scale_dtype", ctypes.c_int32), ("group_size", ctypes.c_int32), ("bits", ctypes.c_int32)]
 
 
 class CcePeerGroup(ctypes.Structure):
@@ -116,6 +123,17 @@ def _load():
     lib.cce_peer_buffer_close.argtypes = [c_vp]
     lib.cce_peer_buffer_free.restype = c_int
     lib.cce_peer_buffer_free.argtypes = [c_vp]
+    lib.cce_forward_q_workspace_bytes.restype = c_sz
+    lib.cce_forward_q_workspace_bytes.argtypes = [c_i64, c_i64, c_i64, c_int]
+    lib.cce_forward_q.restype = c_int
+    lib.cce_forward_q.argtypes = [c_vp, ctypes.POINTER(CceQuantHead), c_vp, c_int, c_vp, c_i64, c_i64, c_i64,
+                                  c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]
+    lib.cce_backward_q_workspace_bytes.restype = c_sz
+    lib.cce_backward_q_workspace_bytes.argtypes = [c_i64, c_i64, c_i64, c_int, c_int]
+    lib.cce_backward_q.restype = c_int
+    lib.cce_backward_q.argtypes = [c_vp, ctypes.POINTER(CceQuantHead), c_vp, c_int, c_vp, c_vp, c_vp, c_vp,
+                                   c_i64, c_i64, c_i64, c_i64, c_int, c_int, c_f, c_vp, c_vp, c_vp, c_vp, c_sz,
+                                   c_vp]
     lib.cce_mma_flops.restype = c_int
     lib.cce_mma_flops.argtypes = [ctypes.POINTER(ctypes.c_uint64), c_int]
     lib.cce_backward_peer.restype = c_int
@@ -376,6 +394,79 @@ def backward(e, c, targets, lse, d_nll, tile_max, bias=None, *, v_offset: int = 
                                   _ptr(skip_stats), _ptr(ws), ws_bytes, _stream(stream))
     _check(rc, what)
     return grad_e, grad_c, grad_b
+
+
+def _quant_head(what, wq, scales, biases, group_size, bits, D):
+    if wq.dim() != 2 or scales.dim() != 2 or biases.shape != scales.shape:
+        raise ValueError(f"[{what}] wq must be 2D and scales / biases 2D of equal shape")
+    if wq.dtype not in (torch.int32, torch.uint32):
+        raise ValueError(f"[{what}] wq must hold 32-bit words, got {wq.dtype}")
+    V = wq.shape[0]
+    if wq.shape[1] * 32 != D * bits or scales.shape != (V, D // group_size):
+        raise ValueError(f"[{what}] quantised head shapes do not match D={D}, bits={bits}, group_size={group_size}")
+    h = CceQuantHead()
+    h.wq, h.scales, h.biases = wq.data_ptr(), scales.data_ptr(), biases.data_ptr()
+    h.scale_dtype = dtype_code(scales.dtype, what)
+    h.group_size, h.bits = int(group_size), int(bits)
+    return h, V
+
+
+def forward_q(e, wq, scales, biases, group_size: int, bits: int, targets, bias=None, stream=None):
+    """Fused forward with a quantised classifier (``cce_forward_q``): the head
+    is expanded one chunk at a time inside the library.  Returns (tile_max, lse, tgt)."""
+    what = "cce_forward_q"
+    if e.dim() != 2:
+        raise ValueError(f"[{what}] e must be [N, D]")
+    N, D = e.shape
+    h, V = _quant_head(what, wq, scales, biases, group_size, bits, D)
+    if targets.dim() != 1 or targets.shape[0] != N or targets.dtype != torch.int32:
+        raise ValueError(f"[{what}] targets must be int32 [N={N}]")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != V):
+        raise ValueError(f"[{what}] bias must be [V={V}]")
+    dev = _require_cuda(what, e=e, wq=wq, scales=scales, biases=biases, targets=targets, bias=bias)
+    dt = dtype_code(e.dtype, what)
+    bdt = dtype_code(bias.dtype, what) if bias is not None else 0
+    ws_bytes = int(lib.cce_forward_q_workspace_bytes(N, D, V, dt))
+    with _alloc_on(stream):
+        tile_max = torch.empty((num_stat_tiles(V), N), dtype=torch.float32, device=dev)
+        lse = torch.empty((N,), dtype=torch.float32, device=dev)
+        tgt = torch.empty((N,), dtype=torch.float32, device=dev)
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    with _Timed("forward", _torch_stream(stream) if _timing is not None else None):
+        rc = lib.cce_forward_q(_ptr(e), ctypes.byref(h), _ptr(bias), bdt, _ptr(targets), N, D, V, 0, dt,
+                               _ptr(tile_max), _ptr(lse), _ptr(tgt), _ptr(ws), ws_bytes, _stream(stream))
+    _check(rc, what)
+    return tile_max, lse, tgt
+
+
+def backward_q(e, wq, scales, biases, group_size: int, bits: int, targets, lse, d_nll, tile_max, bias=None, *,
+               need_e=True, need_bias=False, filter_log_eps: float = FILTER_LOG_EPS, stream=None):
+    """Backward with a quantised (frozen) classifier (``cce_backward_q``).
+    Returns (grad_e in e's dtype or None, grad_bias fp32 or None)."""
+    what = "cce_backward_q"
+    N, D = e.shape
+    h, V = _quant_head(what, wq, scales, biases, group_size, bits, D)
+    dev = _require_cuda(what, e=e, targets=targets, lse=lse, d_nll=d_nll, tile_max=tile_max, bias=bias)
+    if need_bias and bias is None:
+        raise ValueError(f"[{what}] need_bias without bias")
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != V):
+        raise ValueError(f"[{what}] bias must be [V={V}]")
+    if tile_max.numel() != num_stat_tiles(V) * N:
+        raise ValueError(f"[{what}] tile_max must hold {num_stat_tiles(V)}x{N} values")
+    dt = dtype_code(e.dtype, what)
+    bdt = dtype_code(bias.dtype, what) if bias is not None else 0
+    flags = (CCE_NEED_DE if need_e else 0) | (CCE_NEED_DBIAS if need_bias else 0)
+    ws_bytes = int(lib.cce_backward_q_workspace_bytes(N, D, V, dt, flags))
+    with _alloc_on(stream):
+        grad_e = torch.empty((N, D), dtype=e.dtype, device=dev) if need_e else None
+        grad_b = torch.empty((V,), dtype=torch.float32, device=dev) if need_bias else None
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    with _Timed("backward", _torch_stream(stream) if _timing is not None else None):
+        rc = lib.cce_backward_q(_ptr(e), ctypes.byref(h), _ptr(bias), bdt, _ptr(targets), _ptr(lse), _ptr(d_nll),
+                                _ptr(tile_max), N, D, V, 0, dt, flags, float(filter_log_eps), _ptr(grad_e),
+                                _ptr(grad_b), None, _ptr(ws), ws_bytes, _stream(stream))
+    _check(rc, what)
+    return grad_e, grad_b
 
 
 def dequantize(wq, scales, biases, group_size: int, bits: int, dtype, out=None, stream=None):

@@ -2,15 +2,17 @@
 
 The reference's mlx-lm recipe (README.md:84-95) dequantises the whole [V, D]
 head with ``mx.dequantize`` before every call, because its kernels take a
-dense ``c``.  Here the quantised head stays quantised in HBM: the forward and
-the backward expand one vocabulary chunk at a time (``cce_dequantize``) into
-a bounded buffer and run the dense kernels on it with ``v_offset``, exactly
-like one vocabulary shard of the multi-GPU path:
+dense ``c``.  Here the quantised head stays quantised in HBM and the library
+expands it one vocabulary chunk at a time (``cce_forward_q`` /
+``cce_backward_q``): two chunk buffers in the workspace, the next chunk
+expanded on a side stream while the current chunk's GEMMs run, so the
+expansion (HBM-bound) hides behind the tensor-core work:
 
-* forward: per chunk the fused forward gives (tile maxima, lse_k, target
-  logit_k); ``cce_lse_combine`` merges the chunks' (lse_k, tgt_k) rows;
-* backward: per chunk the filtered backward, with the global lse, adds its
-  fp32 grad_e; grad_bias (when the bias requires grad) is per chunk.
+* forward: every chunk's fused forward writes its columns of the tile maxima
+  and of the LSE partials; one fold gives lse for the whole vocabulary;
+* backward: the dense chunk loop (filter mask, dlogits, grad_e accumulated in
+  fp32 across chunks) on the expanded chunks; grad_bias when the bias
+  requires grad.
 
 The quantised weight is frozen (as in LoRA fine-tuning, the recipe's use):
 no gradient flows to ``weight``, ``scales`` or ``biases``.  Layout (MLX's
@@ -80,29 +82,12 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4) -> QuantizedC
                                group_size, bits)
 
 
-def _chunks(V: int, rows: int):
-    rows = max(32, rows // 32 * 32)  # chunk starts stay on statistics-tile boundaries
-    return [(v0, min(V, v0 + rows)) for v0 in range(0, V, rows)]
-
-
 class QuantizedCCEFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, e, weight, scales, biases, bias, targets, valid, reduction, filter_log_eps,
-                group_size, bits, chunk_rows):
-        q = QuantizedClassifier(weight, scales, biases, group_size, bits)
-        V = q.shape[0]
-        chunks = _chunks(V, chunk_rows)
-        buf = None
-        tile_max, part_lse, part_tgt = [], [], []
-        for v0, v1 in chunks:
-            if buf is None or buf.shape[0] != v1 - v0:
-                buf = torch.empty((v1 - v0, e.shape[1]), dtype=e.dtype, device=e.device)
-            q.dequantize(e.dtype, v0, v1, out=buf)
-            tm, l, t = _ext.forward(e, buf, targets, None if bias is None else bias[v0:v1], v_offset=v0)
-            tile_max.append(tm)
-            part_lse.append(l)
-            part_tgt.append(t)
-        lse, _tgt, nll = _ext.lse_combine(torch.stack(part_lse), torch.stack(part_tgt))
+                group_size, bits):
+        tile_max, lse, tgt = _ext.forward_q(e, weight, scales, biases, group_size, bits, targets, bias)
+        nll = lse - tgt
         validf = valid.to(torch.float32)
         per = nll * validf
         count = None
@@ -116,19 +101,17 @@ class QuantizedCCEFunction(torch.autograd.Function):
         ctx.reduction = reduction
         ctx.filter_log_eps = filter_log_eps
         ctx.quant = (group_size, bits)
-        ctx.chunks = chunks
         ctx.has_bias = bias is not None
-        ctx.save_for_backward(e, weight, scales, biases, bias, targets, validf, lse, count,
-                              *tile_max)
+        ctx.save_for_backward(e, weight, scales, biases, bias, targets, validf, lse, count, tile_max)
         ctx.mark_non_differentiable(lse)
         return out, lse
 
     @staticmethod
     def backward(ctx, grad_out, _grad_lse):
-        e, weight, scales, biases, bias, targets, validf, lse, count, *tile_max = ctx.saved_tensors
+        e, weight, scales, biases, bias, targets, validf, lse, count, tile_max = ctx.saved_tensors
         need_e = ctx.needs_input_grad[0]
         need_b = ctx.has_bias and ctx.needs_input_grad[4]
-        none = (None,) * 12
+        none = (None,) * 11
         if grad_out is None or not (need_e or need_b):
             return none
         g = grad_out.to(torch.float32)
@@ -138,34 +121,22 @@ class QuantizedCCEFunction(torch.autograd.Function):
             d_nll = (validf * g).contiguous()
         else:
             d_nll = (validf * (g / count)).contiguous()
-        q = QuantizedClassifier(weight, scales, biases, *ctx.quant)
-        grad_e = torch.zeros(e.shape, dtype=torch.float32, device=e.device) if need_e else None
-        grad_b = torch.empty(bias.shape, dtype=torch.float32, device=e.device) if need_b else None
-        buf = None
-        for (v0, v1), tm in zip(ctx.chunks, tile_max):
-            if buf is None or buf.shape[0] != v1 - v0:
-                buf = torch.empty((v1 - v0, e.shape[1]), dtype=e.dtype, device=e.device)
-            q.dequantize(e.dtype, v0, v1, out=buf)
-            ge, _gc, gb = _ext.backward(e, buf, targets, lse, d_nll, tm,
-                                        None if bias is None else bias[v0:v1], v_offset=v0,
-                                        need_e=need_e, need_c=False, need_bias=need_b,
-                                        grad_e_f32=True, filter_log_eps=ctx.filter_log_eps)
-            if need_e:
-                grad_e += ge
-            if need_b:
-                grad_b[v0:v1] = gb
-        return (grad_e.to(e.dtype) if need_e else None, None, None, None,
-                grad_b.to(bias.dtype) if need_b else None, None, None, None, None, None, None, None)
+        grad_e, grad_b = _ext.backward_q(e, weight, scales, biases, *ctx.quant, targets, lse, d_nll, tile_max,
+                                         bias, need_e=need_e, need_bias=need_b,
+                                         filter_log_eps=ctx.filter_log_eps)
+        return (grad_e, None, None, None, grad_b.to(bias.dtype) if need_b else None, None, None, None, None,
+                None, None)
 
 
 def linear_cross_entropy_quantized(e, c: QuantizedClassifier, targets, bias=None, reduction="mean",
                                    ignore_index=-100, shift=0, return_lse=False, *,
-                                   filter_log_eps=FILTER_LOG_EPS, chunk_rows: int = 16384):
+                                   filter_log_eps=FILTER_LOG_EPS):
     """``linear_cross_entropy`` with a quantised classifier ``c`` (frozen).
 
-    Same arguments and results as ``mlx_cce.linear_cross_entropy``; the head
-    is expanded ``chunk_rows`` vocabulary rows at a time, in e's dtype, and
-    never as a whole [V, D] tensor.
+    Same arguments and results as ``mlx_cce.linear_cross_entropy``; the
+    library expands the head one vocabulary chunk at a time, in e's dtype, on
+    a side stream while the previous chunk's GEMMs run, and never as a whole
+    [V, D] tensor.
     """
     if reduction not in REDUCTIONS:
         raise ValueError(f"Unknown reduction: {reduction}")
@@ -185,8 +156,7 @@ def linear_cross_entropy_quantized(e, c: QuantizedClassifier, targets, bias=None
     loss, lse = QuantizedCCEFunction.apply(e2, c.weight.contiguous(), c.scales.contiguous(),
                                            c.biases.contiguous(),
                                            None if bias is None else bias.contiguous(), safe, valid,
-                                           reduction, filter_log_eps, int(c.group_size), int(c.bits),
-                                           int(chunk_rows))
+                                           reduction, filter_log_eps, int(c.group_size), int(c.bits))
     if reduction == "none":
         loss = loss.reshape(orig_shape)
     return (loss, lse) if return_lse else loss

@@ -48,7 +48,10 @@ def test_dequantize_kernel_matches_oracle(bits, group, scale_dtype, out_dtype):
 
 
 @pytest.mark.parametrize("reduction", ["mean", "none"])
-def test_quantized_cce_matches_dense_and_oracle(reduction):
+def test_quantized_cce_matches_dense_and_oracle(reduction, monkeypatch):
+    # backward chunks of 1024 rows: five, the last one ragged; the library
+    # expands each into one of its two chunk buffers while the previous runs
+    monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "1024")
     dev = _dev()
     N, D, V = 300, 256, 5000
     q, wq = _quantized(V, D, 64, 4, torch.bfloat16, seed=7)
@@ -68,8 +71,7 @@ def test_quantized_cce_matches_dense_and_oracle(reduction):
         return (loss.detach().double().cpu().numpy(), e_.grad.double().cpu().numpy(),
                 b_.grad.double().cpu().numpy())
 
-    # chunks of 1024 rows: five, the last one ragged
-    lq, eq, bq = run(lambda *a, **k: mlx_cce.linear_cross_entropy_quantized(*a, **k, chunk_rows=1024), q)
+    lq, eq, bq = run(mlx_cce.linear_cross_entropy_quantized, q)
     c_dense = q.dequantize(torch.bfloat16)
     ld, ed, bd = run(mlx_cce.linear_cross_entropy, c_dense)
     np.testing.assert_allclose(lq, ld, rtol=1e-5, atol=1e-6)
@@ -82,3 +84,32 @@ def test_quantized_cce_matches_dense_and_oracle(reduction):
     np.testing.assert_allclose(lq.reshape(-1), np.asarray(loss).reshape(-1), rtol=1e-3, atol=1e-6)
     assert O.rel_max_abs(eq, dE) < GRAD_TOL
     assert O.rel_max_abs(bq, dB) < GRAD_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_quantized_head_several_forward_chunks(dtype, monkeypatch):
+    """V = 40000 spans three 16384-row forward chunks (the last one ragged)
+    and five 8192-row backward chunks; bf16 runs on the tensor cores, float32
+    on the CUDA cores.  Against the dense path on the same dequantised head."""
+    monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "8192")
+    dev = _dev()
+    N, D, V = 256, 128, 40000
+    q, _wq = _quantized(V, D, 32, 8, torch.float16, seed=9)
+    g = torch.Generator().manual_seed(10)
+    e = torch.randn(N, D, generator=g).to(dtype)
+    t = torch.randint(0, V, (N,), generator=g)
+    t[::9] = -100
+    t[1] = V - 1
+
+    def run(fn, c):
+        e_ = e.to(dev).requires_grad_(True)
+        loss, lse = fn(e_, c, t.to(dev), reduction="sum", return_lse=True)
+        loss.backward()
+        torch.cuda.synchronize()
+        return loss.item(), lse.double().cpu().numpy(), e_.grad.double().cpu().numpy()
+
+    lq, lseq, eq = run(mlx_cce.linear_cross_entropy_quantized, q)
+    ld, lsed, ed = run(mlx_cce.linear_cross_entropy, q.dequantize(dtype))
+    np.testing.assert_allclose(lq, ld, rtol=1e-5)
+    np.testing.assert_allclose(lseq, lsed, rtol=1e-5)
+    assert O.rel_max_abs(eq, ed) < 1e-2
