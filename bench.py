@@ -470,24 +470,35 @@ def run_ours(args, rank, world, local_rank):
     # data loader, step i + 1's inputs are copied on a copy stream (into the
     # other of two device buffers) while step i computes; a buffer is
     # overwritten only after the loss read-back of the step that last read it.
-    e_host = e_cpu.pin_memory()
+    # With N GPUs every rank needs all of e: each copies its 1/N of the rows
+    # over PCIe and the rows are all-gathered over NVLink (NCCL) in the step,
+    # so the job moves e across PCIe once, not N times.
+    split = world > 1 and N % world == 0
+    rows = N // world if split else N
+    e_host = (e_cpu[rank * rows:(rank + 1) * rows] if split else e_cpu).contiguous().pin_memory()
     t_host = t_cpu.pin_memory()
     e_dev = [torch.empty_like(e), torch.empty_like(e)]
+    e_part = [torch.empty((rows, D), dtype=e.dtype, device=dev) for _ in range(2)] if split else e_dev
     t_dev = [torch.empty_like(t), torch.empty_like(t)]
     copy_stream = torch.cuda.Stream(device=dev)
     ready = [torch.cuda.Event(), torch.cuda.Event()]
 
     def prefetch(i):
         with torch.cuda.stream(copy_stream):
-            e_dev[i % 2].copy_(e_host, non_blocking=True)
+            e_part[i % 2].copy_(e_host, non_blocking=True)
             t_dev[i % 2].copy_(t_host, non_blocking=True)
             ready[i % 2].record(copy_stream)
 
-    # one untimed pass of the loop body (its buffers and copies warm)
+    def inputs(i):
+        torch.cuda.current_stream().wait_event(ready[i % 2])
+        if split:
+            dist.all_gather_into_tensor(e_dev[i % 2], e_part[i % 2])
+        return e_dev[i % 2], t_dev[i % 2]
+
+    # two untimed passes of the loop body (its buffers, copies and collective warm)
     for i in range(2):
         prefetch(i)
-        torch.cuda.current_stream().wait_event(ready[i % 2])
-        step(e_dev[i % 2], t_dev[i % 2]).detach().cpu()
+        step(*inputs(i)).detach().cpu()
     barrier()
     ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev2.record()
@@ -495,8 +506,7 @@ def run_ours(args, rank, world, local_rank):
     d2h = 0
     prefetch(0)
     for i in range(args.steps):
-        torch.cuda.current_stream().wait_event(ready[i % 2])
-        loss = step(e_dev[i % 2], t_dev[i % 2])
+        loss = step(*inputs(i))
         if i + 1 < args.steps:
             prefetch(i + 1)
         host = loss.detach().cpu()
@@ -504,7 +514,11 @@ def run_ours(args, rank, world, local_rank):
     ev3.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
-    h2d = e_host.numel() * e_host.element_size() + t_host.numel() * t_host.element_size()
+    # bytes the whole job moves per step: e once (split over the ranks), the
+    # targets to every rank; the loss back to the host on every rank
+    h2d = e_cpu.numel() * e_cpu.element_size() * (1 if split else world) + \
+        t_host.numel() * t_host.element_size() * world
+    d2h *= world
 
     # ---- parity of the benchmarked step (every rank, every N) ----
     parity = None

@@ -150,12 +150,14 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   const int64_t elt = tc ? 2 : 4;
   const int64_t nrow = N > 0 ? N : 1;
   const int64_t target = target_chunk_rows();
-  int64_t budget = nrow * elt * target;
+  // the budget is in 16-bit bytes for both paths (the CUDA-core path's fp32
+  // dlogits get half the rows), so neither plan's workspace dominates the other's
+  int64_t budget = nrow * 2 * target;
   if (budget > kDlMaxBytes) budget = kDlMaxBytes;
   if (budget < kDlMinBytes && target == kDlTargetRows) budget = kDlMinBytes;
   int64_t vc = (budget / (nrow * elt)) / gran * gran;
   if (vc < gran) vc = gran;
-  if (target == kDlTargetRows && nrow * elt * target < kDlSmallNBytes) {
+  if (target == kDlTargetRows && nrow * 2 * target < kDlSmallNBytes) {
     // small N: longer chunks, up to 256 MiB and half the vocabulary
     const int64_t half = cce::round_up(cce::ceil_div(V > 0 ? V : 1, 2), gran);
     int64_t grow = (kDlSmallNBytes / (nrow * elt)) / gran * gran;
