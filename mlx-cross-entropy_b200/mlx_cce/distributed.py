@@ -9,8 +9,12 @@ steps, both through ``torch.distributed`` (NCCL over NVLink on B200):
 * forward: one ``all_gather_into_tensor`` of the [2, N] fp32 (lse_r, tgt_r)
   rows, merged on every rank by the ``cce_lse_combine`` kernel, so every rank
   holds the identical loss;
-* backward: one ``all_reduce(SUM)`` of the fp32 grad_e partials; grad_c and
-  grad_bias stay sharded.
+* backward: grad_e is summed across the ranks inside the library's backward
+  (``cce_backward_peer``): the last grad_e GEMM of each rank stores its fp32
+  tiles into the exchange buffer of the rank that owns those rows over NVLink
+  peer memory, owners reduce in rank order and every rank gathers the summed
+  rows.  ``CCE_GRAD_E_EXCHANGE=nccl`` selects the unfused baseline instead
+  (fp32 partials, one NCCL ``all_reduce``).  grad_c and grad_bias stay sharded.
 
 The reference has no multi-device code; this is the build's own addition for
 the multi-GPU rows of the benchmark.
