@@ -181,6 +181,24 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
   }
 }
 
+// grad_c rows of a vocabulary chunk's 128-row M tiles that no kept block
+// reaches are zero.  One block per M tile: its row of the transposed mask
+// table (bit = row block) is tested, and a dead tile's rows are written with
+// 16-byte zero stores (rows are whole multiples of 16 bytes).
+__global__ void __launch_bounds__(256)
+zero_dead_mtiles_kernel(const uint32_t* __restrict__ keep_t, int64_t ld, int words, int64_t rows,
+                        int64_t row_bytes, char* __restrict__ out) {
+  const int64_t m = blockIdx.x;
+  int live = 0;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) live |= keep_t[m * ld + w] != 0u;
+  if (__syncthreads_or(live)) return;
+  const int64_t r0 = m * 128;
+  const int64_t r1 = r0 + 128 < rows ? r0 + 128 : rows;
+  uint4* dst = reinterpret_cast<uint4*>(out + r0 * row_bytes);
+  const int64_t n = (r1 - r0) * row_bytes / 16;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 template <typename T>
 __global__ void cast_f32_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -314,39 +332,84 @@ cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype
   return launched();
 }
 
-// Affine group dequantisation: one thread per packed word, its 32 / BITS values
-// share one group (group_size >= 32 >= 32 / BITS), so one scale and bias.
+// The kPer values of one packed word written to dst: one or two 16-byte
+// stores (8-byte for 8-bit words into 16-bit outputs) when `vec` (dst is
+// aligned to the word's output bytes), else element by element.
+template <typename TO, int kPer>
+__device__ __forceinline__ void store_values(TO* dst, const float (&v)[kPer], bool vec) {
+  constexpr int kBytes = kPer * (int)sizeof(TO);
+  if (vec) {
+    uint32_t u[kBytes / 4];
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) u[i] = __float_as_uint(v[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kPer / 2; ++i) {
+        TO lo = from_f32<TO>(v[2 * i]), hi = from_f32<TO>(v[2 * i + 1]);
+        u[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+      }
+    }
+    if constexpr (kBytes % 16 == 0) {
+#pragma unroll
+      for (int k = 0; k < kBytes / 16; ++k)
+        reinterpret_cast<uint4*>(dst)[k] = make_uint4(u[4 * k], u[4 * k + 1], u[4 * k + 2], u[4 * k + 3]);
+    } else {
+      static_assert(kBytes % 8 == 0, "a packed word's values fill whole 8-byte units");
+#pragma unroll
+      for (int k = 0; k < kBytes / 8; ++k) reinterpret_cast<uint2*>(dst)[k] = make_uint2(u[2 * k], u[2 * k + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) dst[i] = from_f32<TO>(v[i]);
+  }
+}
+
+// Affine group dequantisation.  A block walks whole rows; thread t takes
+// packed words t, t + blockDim.x, ... of a row, so a warp reads 128
+// contiguous bytes and writes its values as contiguous vector stores.  A
+// word's 32 / BITS values share one group (group_size >= 32 >= 32 / BITS):
+// one scale and one bias, found by a shift (group_size is a power of two).
 template <int BITS, typename TS, typename TO>
-__global__ void dequant_kernel(const uint32_t* __restrict__ wq, const TS* __restrict__ scales,
-                               const TS* __restrict__ biases, int64_t words, int64_t wpr, int64_t gpr,
-                               int group, TO* __restrict__ out) {
+__global__ void __launch_bounds__(256)
+dequant_kernel(const uint32_t* __restrict__ wq, const TS* __restrict__ scales, const TS* __restrict__ biases,
+               int64_t rows, int wpr, int gpr, int gshift, bool vec, TO* __restrict__ out) {
   constexpr int kPer = 32 / BITS;
   constexpr uint32_t kMask = (1u << BITS) - 1u;
-  for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words;
-       w += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = w / wpr;
-    const int64_t j0 = (w - r * wpr) * kPer;  // first value of the word within the row
-    const int64_t g = r * gpr + j0 / group;
-    const float s = to_f32(scales[g]), b = to_f32(biases[g]);
-    const uint32_t q = __ldg(wq + w);
-    TO* dst = out + r * (wpr * kPer) + j0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint32_t* src = wq + r * wpr;
+    const TS* sr = scales + r * gpr;
+    const TS* br = biases + r * gpr;
+    TO* dst = out + r * (int64_t)wpr * kPer;
+    for (int w = threadIdx.x; w < wpr; w += blockDim.x) {
+      const int g = (w * kPer) >> gshift;
+      const float s = to_f32(sr[g]), b = to_f32(br[g]);
+      const uint32_t q = __ldg(src + w);
+      float v[kPer];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) dst[i] = from_f32<TO>(fmaf(s, (float)((q >> (i * BITS)) & kMask), b));
+      for (int i = 0; i < kPer; ++i) v[i] = fmaf(s, (float)((q >> (i * BITS)) & kMask), b);
+      store_values<TO, kPer>(dst + w * kPer, v, vec);
+    }
   }
 }
 
 template <typename TS, typename TO>
 cudaError_t dequant_dispatch(const uint32_t* wq, const void* scales, const void* biases, int64_t rows,
                              int64_t D, int group, int bits, void* out, cudaStream_t stream) {
-  const int64_t wpr = D * bits / 32, gpr = D / group, words = rows * wpr;
-  const int grid = grid_for(words, 256);
+  const int wpr = (int)(D * bits / 32), gpr = (int)(D / group);
+  const int gshift = group == 32 ? 5 : group == 64 ? 6 : 7;
+  // rows start on 16-byte boundaries when the output does (D is a multiple
+  // of the group size, >= 32 values)
+  const bool vec = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  int64_t grid = rows < 148 * 8 ? rows : 148 * 8;
+  if (grid < 1) grid = 1;
   const TS* s = static_cast<const TS*>(scales);
   const TS* b = static_cast<const TS*>(biases);
   TO* o = static_cast<TO*>(out);
   switch (bits) {
-    case 2: dequant_kernel<2, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
-    case 4: dequant_kernel<4, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
-    case 8: dequant_kernel<8, TS, TO><<<grid, 256, 0, stream>>>(wq, s, b, words, wpr, gpr, group, o); break;
+    case 2: dequant_kernel<2, TS, TO><<<(unsigned)grid, 256, 0, stream>>>(wq, s, b, rows, wpr, gpr, gshift, vec, o); break;
+    case 4: dequant_kernel<4, TS, TO><<<(unsigned)grid, 256, 0, stream>>>(wq, s, b, rows, wpr, gpr, gshift, vec, o); break;
+    case 8: dequant_kernel<8, TS, TO><<<(unsigned)grid, 256, 0, stream>>>(wq, s, b, rows, wpr, gpr, gshift, vec, o); break;
     default: return cudaErrorInvalidValue;
   }
   return launched();
@@ -373,6 +436,15 @@ cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void
     case CCE_BF16: return dequant_out<__nv_bfloat16>(wq, scales, biases, rows, D, group, bits, out_dtype, out, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_zero_dead_mtiles(const uint32_t* keep_t, int64_t ld, int words, int64_t rows, int64_t row_bytes,
+                                    void* out, cudaStream_t stream) {
+  const int64_t tiles = ceil_div(rows, 128);
+  if (tiles == 0) return cudaSuccess;
+  zero_dead_mtiles_kernel<<<(unsigned)tiles, 256, 0, stream>>>(keep_t, ld, words, rows, row_bytes,
+                                                               static_cast<char*>(out));
+  return launched();
 }
 
 cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream) {

@@ -59,6 +59,7 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
+constexpr int kMaxClaim = 16;                    // most unit ids one scheduler atomic claims
 // Statistics tiles (kStatTile vocabulary columns each, the filter's column
 // granularity) per engine tile and per K-block.
 constexpr int kGroups = BN / kStatTile;                // per 256-column output tile
@@ -77,6 +78,14 @@ constexpr int kPushWaitCode = 8;  // status code: a push unit's epilogue threads
 // costs on its own, so longer runs load the whole tile in one box.
 constexpr uint32_t kNarrowMaxGroups = 2;
 constexpr uint32_t B32_BYTES = kStatTile * BK * 2;  // 4 KB: 32 rows x 128 bytes
+// Half K-blocks (kHalfK epilogues): a K-block whose only kept statistics tile
+// is one of its two 32-row halves loads that half alone -- A as a 128 x 32
+// box in the 64-byte swizzle (SW64 K-major), B as a 3-D box of 32 K-rows x
+// 256 columns (four 4 KB slabs) -- into the first half of the stage.
+constexpr uint32_t A_HALF_BYTES = BM * (BK / 2) * 2;  // 8 KB
+constexpr uint32_t B_HALF_BYTES = BN * (BK / 2) * 2;  // 16 KB
+constexpr uint32_t BOX_MN_HALF_BYTES = 64 * (BK / 2) * 2;  // one 64-column slab of a half box (4 KB)
+static_assert(BK / 2 == kStatTile, "a half K-block is one statistics tile");
 
 // Executed tensor-core work per kernel kind (0 forward, 1 dlogits, 2 grad_e,
 // 3 grad_c): the sum of N over every issued M = 128, K = 16 MMA, added once
@@ -192,6 +201,7 @@ struct Stager {
 template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr int kKind = 0;  // slot in g_mma_cols
   const int32_t* targets;
   const void* bias;
@@ -210,6 +220,7 @@ struct FwdEpi {
   static constexpr bool kMask = false;
   static constexpr bool kZeroTiles = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
+  __device__ __forceinline__ bool skip_unit(const MaskView&, int, int, int, int) const { return false; }
   __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
   __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
   __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
@@ -276,6 +287,7 @@ struct FwdEpi {
 template <typename T, typename TB>
 struct DlogitsEpi {
   static constexpr bool kNarrowB = true;  // B rows loaded for a tile's live column run only
+  static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr int kKind = 1;  // slot in g_mma_cols
   const int32_t* targets;
   const float* lse;
@@ -305,6 +317,10 @@ struct DlogitsEpi {
   }
   __device__ __forceinline__ bool tile_active(const MaskView& mk, int mb, int nb) const {
     return group_mask(mk, mb, nb) != 0;
+  }
+  // Tiles without a kept block produce nothing: the producer passes them over.
+  __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int, int) const {
+    return !tile_active(mk, mb, nb);
   }
   // Column groups the MMA computes: only the kept ones (the epilogue never
   // reads the accumulator columns of the others).
@@ -387,6 +403,7 @@ struct DlogitsEpi {
 // unit raises the `pushed` flag on every rank.  The slabs are not written.
 struct GradEEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kHalfK = true;  // half K-blocks loaded alone when half_k is set
   static constexpr int kKind = 2;  // slot in g_mma_cols
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
@@ -399,6 +416,7 @@ struct GradEEpi {
   unsigned total_units;     // work units of the launch
   peer::Peers peers;
   peer::Layout layout;
+  int half_k;               // the half-K maps are valid: load half K-blocks alone
 
   struct State {
     int64_t col0;
@@ -442,6 +460,12 @@ struct GradEEpi {
     const int lim = min(kSpk * kb1, mask_cols);
     const int t = mk.next(mb, kSpk * kb, lim);
     return t < lim ? t / kSpk : kb1;
+  }
+  // A unit no K-block reaches adds zeros to the slab after the first chunk:
+  // nothing to do, so the producer passes it over (not in push mode, where
+  // every unit sends its slab, nor in the first chunk, which zeroes it).
+  __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int kb0, int kb1) const {
+    return accumulate && !push && next_kb(mk, mb, nb, kb0, kb1) >= kb1;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   template <class S>
@@ -517,6 +541,7 @@ struct GradEEpi {
 template <typename T>
 struct GradCEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr int kKind = 3;  // slot in g_mma_cols
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
@@ -547,6 +572,13 @@ struct GradCEpi {
     const int r = mk.next(mb, kb / kKpr, lim);
     if (r >= lim) return kb1;
     return max(kb, r * kKpr);
+  }
+  // An M tile no K-block reaches (no kept block in its 128 vocabulary rows)
+  // is zeroed beforehand by zero_dead_mtiles when `dead_zeroed` is set: the
+  // producer passes its units over.
+  int dead_zeroed;
+  __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int kb0, int kb1) const {
+    return dead_zeroed && next_kb(mk, mb, nb, kb0, kb1) >= kb1;
   }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ bool zero_shortcut() const { return true; }
@@ -631,8 +663,10 @@ __device__ __forceinline__ void load_mask_view(const Epi& epi, uint8_t* smask, M
 template <bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmB32, const __grid_constant__ CUtensorMap tmC,
-               const Sched sched, const Epi epi, const uint32_t idesc) {
+               const __grid_constant__ CUtensorMap tmAalt, const __grid_constant__ CUtensorMap tmBalt,
+               const __grid_constant__ CUtensorMap tmC, const Sched sched, const Epi epi, const uint32_t idesc) {
+  // tmBalt: K-major B in 32-row boxes (kNarrowB); tmAalt / tmBalt: the half
+  // K-block boxes of A and B (kHalfK).
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -671,7 +705,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if constexpr (Epi::kNarrowB) prefetch_tmap(&tmB32);
+    if constexpr (Epi::kNarrowB) prefetch_tmap(&tmBalt);
+    if constexpr (Epi::kHalfK) {
+      if (epi.half_k) {
+        prefetch_tmap(&tmAalt);
+        prefetch_tmap(&tmBalt);
+      }
+    }
   }
   // Filter-mask slice: copied to shared memory when it fits, else read in place.
   MaskView mk{nullptr, nullptr, 0, 0, 0};
@@ -690,20 +730,48 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      // the next tile id is fetched one tile ahead so the atomic's latency
-      // overlaps the current tile's loads
+      // Work units are claimed from the global counter (dynamic schedule) or
+      // in a fixed stride (static).  The next id is claimed one unit ahead, so
+      // the atomic's latency overlaps the current unit's loads.  A unit the
+      // epilogue has nothing to do for (Epi::skip_unit) is passed over here
+      // and never reaches the MMA and epilogue warps; after a passed-over unit
+      // the next claim takes twice as many ids (up to kMaxClaim), after a live
+      // one a single id, so long runs of dead units cost few atomics while
+      // live units stay balanced across the SMs.
       int next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x;
+      int nend = next + 1;  // claimed ids [next, nend)
+      int sidx = 0;         // static schedule: claims made
+      int batch = 1;
+      auto advance = [&](bool skipped) {
+        if (++next < nend) return;
+        if (sched.counter) {
+          batch = skipped ? (batch * 2 < kMaxClaim ? batch * 2 : kMaxClaim) : 1;
+          next = atomicAdd(sched.counter, batch);
+          nend = next + batch;
+        } else {
+          next = (int)blockIdx.x + (++sidx) * (int)gridDim.x;
+          nend = next + 1;
+        }
+      };
       for (int i = 0;; ++i) {
         const int slot = i & (RING - 1);
         if (!mbar_wait(rempty + slot, ((i / RING) & 1) ^ 1u, 5)) break;
-        const int tile = next < num_tiles ? next : -1;
+        int tile = -1;
+        int mb = 0, nb = 0, ks = 0, kb0 = 0, kb1 = 0;
+        while (next < num_tiles) {
+          const int u = next;
+          sched.coords(u, mb, nb, ks);
+          sched.krange(ks, kb0, kb1);
+          const bool skip = epi.skip_unit(mk, mb, nb, kb0, kb1);
+          advance(skip);
+          if (!skip) {
+            tile = u;
+            break;
+          }
+        }
         ring[slot] = tile;
         mbar_arrive(rfull + slot);
         if (tile < 0) break;
-        next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (i + 1) * (int)gridDim.x;
-        int mb, nb, ks, kb0, kb1;
-        sched.coords(tile, mb, nb, ks);
-        sched.krange(ks, kb0, kb1);
         if (!epi.tile_active(mk, mb, nb)) continue;
         // B rows to load: the whole tile, or (K-major B, kNarrowB) only a
         // short run of live 32-column groups [nj0, nj0 + nn0) -- the rows
@@ -724,10 +792,25 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         bool ok = true;
         for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(full + stage, tx_bytes);
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
           const int k0 = kb * BK;
+          if constexpr (Epi::kHalfK) {
+            // one kept statistics tile (ksub_mask 0x3 or 0xC): load that half only
+            const uint32_t km = epi.half_k ? epi.ksub_mask(mk, mb, nb, kb) : 0xFu;
+            if (km != 0xFu) {
+              const int kh = k0 + (km == 0x3u ? 0 : BK / 2);
+              mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + B_HALF_BYTES);
+              tma_load_2d(a, &tmAalt, full + stage, kh, mb * BM);
+              tma_load_3d(b, &tmBalt, full + stage, 0, kh, nb * (BN / 64));
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
+            }
+          }
+          mbar_arrive_expect_tx(full + stage, tx_bytes);
           if (A_MN) {
             if (sched.a3d) {
               tma_load_3d(a, &tmA, full + stage, 0, k0, mb * (BM / 64));
@@ -748,7 +831,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
           } else if (nn0 < (uint32_t)kGroups) {
             for (uint32_t g = nj0; g < nj0 + nn0; ++g)
-              tma_load_2d(b + g * B32_BYTES, &tmB32, full + stage, k0, nb * BN + (int)(g * kStatTile));
+              tma_load_2d(b + g * B32_BYTES, &tmBalt, full + stage, k0, nb * BN + (int)(g * kStatTile));
           } else {
             tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
           }
@@ -776,6 +859,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                    : smem_desc(smem_u32(sB), 16, 1024);
       constexpr uint32_t a_kstep = (A_MN ? 2048u : 32u) >> 4;
       constexpr uint32_t b_kstep = (B_MN ? 2048u : 32u) >> 4;
+      // half K-blocks (kHalfK: K-major A, MN-major B): A in the 64-byte
+      // swizzle (8-row groups 512 bytes apart), B slabs 4 KB apart
+      const uint64_t adesc_h = smem_desc_sw64(smem_u32(sA), 16, 512);
+      const uint64_t bdesc_h = smem_desc(smem_u32(sB), BOX_MN_HALF_BYTES, 1024);
       for (int i = 0;; ++i) {
         const int slot = i & (RING - 1);
         if (!mbar_wait(rfull + slot, (i / RING) & 1, 6)) break;
@@ -816,6 +903,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           mma_cols += (unsigned long long)(__popc(km & 0xFu) * kStatTile * n0);
           if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
           tc_fence_after();
+          if constexpr (Epi::kHalfK) {
+            if (epi.half_k && km != 0xFu) {
+              // the stage holds the kept half: its two K=16 steps
+              const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
+              const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4) + boff;
+#pragma unroll
+              for (int k = 0; k < BK / 32; ++k) {
+                mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
+                fresh = 0;
+              }
+              mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
+            }
+          }
           const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
           const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4) + boff;
 #pragma unroll
@@ -943,7 +1048,8 @@ int num_sms() {
 // Row-major [outer][inner] 16-bit matrix with row stride `ld` elements, read in
 // (box_inner x box_outer) boxes with 128-byte swizzling and zero fill.
 bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int64_t outer, int64_t ld,
-               uint32_t box_inner, uint32_t box_outer) {
+               uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
@@ -952,9 +1058,18 @@ bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int6
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(tm, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// CCE_GRAD_E_HALF_K=0 in the environment makes grad_e load whole K-blocks
+// only (an A/B switch for timing; read once).
+bool half_k_enabled() {
+  static const bool v = [] {
+    const char* s = getenv("CCE_GRAD_E_HALF_K");
+    return !(s != nullptr && s[0] == '0');
+  }();
+  return v;
 }
 
 // An MN-major operand [outer][inner] (inner contiguous, a multiple of 64) as a
@@ -1043,8 +1158,9 @@ cudaError_t ensure_smem_attr(K kern, size_t bytes, std::atomic<unsigned long lon
 }
 
 template <bool A_MN, bool B_MN, class Epi>
-cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmB32,
-                        const CUtensorMap& tmC, const Sched& s, const Epi& epi, bool bf16, cudaStream_t stream) {
+cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmAalt,
+                        const CUtensorMap& tmBalt, const CUtensorMap& tmC, const Sched& s, const Epi& epi,
+                        bool bf16, cudaStream_t stream) {
   auto kern = tc_gemm_kernel<A_MN, B_MN, Epi>;
   static std::atomic<unsigned long long> attr_ctx[64];
   cudaError_t err = ensure_smem_attr(kern, SMEM_BYTES, attr_ctx);
@@ -1053,7 +1169,7 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmB32, tmC, s, epi, idesc);
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmAalt, tmBalt, tmC, s, epi, idesc);
   return launched();
 }
 
@@ -1085,7 +1201,7 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
            nullptr, raster_group(a.N * a.D * 2)};
   FwdEpi<TB> epi{a.targets, a.bias, a.tile_max, a.part_m, a.part_s, a.tgt, a.N, a.V, a.v_offset};
   const CUtensorMap tmC{};  // the forward epilogue writes no tiles
-  return launch_gemm<false, false>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, false>(tmA, tmB, tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 template <typename T, typename TB>
@@ -1105,7 +1221,7 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   CUtensorMap tmC, tmB32;
   if (!make_tmap_out(&tmC, a.dlogits, a.dtype, a.vc_len, a.N, a.vc_ld)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB32, cchunk, bf16, a.D, a.vc_len, a.D, BK, kStatTile)) return cudaErrorInvalidValue;
-  return launch_gemm<false, false>(tmA, tmB, tmB32, tmC, sc, epi, bf16, s);
+  return launch_gemm<false, false>(tmA, tmB, tmA, tmB32, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace
@@ -1162,7 +1278,14 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
     epi.peers = push->peers;
     epi.layout = push->layout;
   }
-  return launch_gemm<false, true>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
+  // half K-block boxes: A (dlogits) 32 columns wide in the 64-byte swizzle,
+  // B (the c chunk) 32 rows of the 3-D MN-major form
+  CUtensorMap tmAh = tmA, tmBh = tmB;
+  epi.half_k = (b3d && half_k_enabled() &&
+                make_tmap(&tmAh, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+                make_tmap_mn3d(&tmBh, cchunk, bf16, a.D, a.vc_len, a.D, BK / 2, BN / 64))
+                   ? 1 : 0;
+  return launch_gemm<false, true>(tmA, tmB, tmAh, tmBh, tmC, sc, epi, bf16, s);
 }
 
 template <typename T>
@@ -1178,10 +1301,16 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
                   a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
                   (int)ceil_div(a.vc_len, (int64_t)128), (int)ceil_div(a.N, kRowBlock),
                   a.vc_len, a.D};
+  // dead M tiles are zeroed by a plain store kernel first; the GEMM passes them over
+  const cudaError_t zerr = launch_zero_dead_mtiles(a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
+                                                   (int)ceil_div(ceil_div(a.N, kRowBlock), 32), a.vc_len,
+                                                   a.D * (int64_t)sizeof(T), epi.out, s);
+  if (zerr != cudaSuccess) return zerr;
+  epi.dead_zeroed = 1;
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;
-  return launch_gemm<true, true>(tmA, tmB, tmB, tmC, sc, epi, bf16, s);
+  return launch_gemm<true, true>(tmA, tmB, tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
 }  // namespace

@@ -218,6 +218,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// The same for a 64-byte-swizzled operand tile (layout SWIZZLE_64B).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (smem_desc(saddr, lbo, sbo) & ~(static_cast<uint64_t>(7) << 61)) | (static_cast<uint64_t>(4) << 61);
+}
+
 // Instruction descriptor of kind::f16 with fp32 accumulation.
 __host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool bf16, bool a_mn, bool b_mn) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
