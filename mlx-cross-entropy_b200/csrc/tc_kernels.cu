@@ -59,7 +59,7 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
-constexpr int kMaxClaim = 16;                    // most unit ids one scheduler atomic claims
+constexpr int kMaxClaim = 16;                    // default most unit ids one scheduler atomic claims
 // Statistics tiles (kStatTile vocabulary columns each, the filter's column
 // granularity) per engine tile and per K-block.
 constexpr int kGroups = BN / kStatTile;                // per 256-column output tile
@@ -735,7 +735,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // the atomic's latency overlaps the current unit's loads.  A unit the
       // epilogue has nothing to do for (Epi::skip_unit) is passed over here
       // and never reaches the MMA and epilogue warps; after a passed-over unit
-      // the next claim takes twice as many ids (up to kMaxClaim), after a live
+      // the next claim takes twice as many ids (up to sched.max_claim), after a live
       // one a single id, so long runs of dead units cost few atomics while
       // live units stay balanced across the SMs.
       int next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x;
@@ -745,7 +745,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       auto advance = [&](bool skipped) {
         if (++next < nend) return;
         if (sched.counter) {
-          batch = skipped ? (batch * 2 < kMaxClaim ? batch * 2 : kMaxClaim) : 1;
+          batch = skipped ? (batch * 2 < sched.max_claim ? batch * 2 : (sched.max_claim > 1 ? sched.max_claim : 1)) : 1;
           next = atomicAdd(sched.counter, batch);
           nend = next + batch;
         } else {
@@ -978,17 +978,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (zero_tile) {
         if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
       } else {
+        // the TMEM load of chunk c + 1 is in flight while chunk c is processed
+        uint32_t cur[32], nxt[32];
+        bool cur_live = any_kb && epi.chunk_live(st, 0);
+        if (cur_live) tmem_ld32_issue(tbase, cur);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
           __syncwarp();
-          if (any_kb && epi.chunk_live(st, c)) {
-            tmem_ld32(tbase + c * 32, v);
-          } else {
+          const bool nxt_live = c + 1 < BN / 32 && any_kb && epi.chunk_live(st, c + 1);
+          if (cur_live) tmem_ld_wait(cur);
+          if (nxt_live) tmem_ld32_issue(tbase + (c + 1) * 32, nxt);
+          float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-          }
+          for (int j = 0; j < 32; ++j) v[j] = cur_live ? __uint_as_float(cur[j]) : 0.f;
           epi.chunk(st, c, v, sg);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+          cur_live = nxt_live;
         }
       }
       epi.end(st);
@@ -1062,12 +1068,28 @@ bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int6
   return r == CUDA_SUCCESS;
 }
 
-// CCE_GRAD_E_HALF_K=0 in the environment makes grad_e load whole K-blocks
-// only (an A/B switch for timing; read once).
+// A/B switches for timing, read once from the environment:
+// CCE_GRAD_E_HALF_K=0 makes grad_e load whole K-blocks only;
+// CCE_GRAD_C_ZERO_KERNEL=0 leaves grad_c's dead M tiles to the GEMM's
+// epilogue (plain zero stores per tile) instead of a zeroing kernel;
+// CCE_SCHED_MAX_CLAIM=<n> caps the ids one scheduler claim takes (default 16).
+bool env_flag(const char* name, bool dflt) {
+  const char* s = getenv(name);
+  return s == nullptr || s[0] == 0 ? dflt : s[0] != '0';
+}
 bool half_k_enabled() {
-  static const bool v = [] {
-    const char* s = getenv("CCE_GRAD_E_HALF_K");
-    return !(s != nullptr && s[0] == '0');
+  static const bool v = env_flag("CCE_GRAD_E_HALF_K", true);
+  return v;
+}
+bool zero_kernel_enabled() {
+  static const bool v = env_flag("CCE_GRAD_C_ZERO_KERNEL", true);
+  return v;
+}
+int max_claim() {
+  static const int v = [] {
+    const char* s = getenv("CCE_SCHED_MAX_CLAIM");
+    const int n = s ? atoi(s) : 0;
+    return n >= 1 && n <= 64 ? n : kMaxClaim;
   }();
   return v;
 }
@@ -1169,7 +1191,9 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmAalt, tmBalt, tmC, s, epi, idesc);
+  Sched sc = s;
+  sc.max_claim = max_claim();
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmAalt, tmBalt, tmC, sc, epi, idesc);
   return launched();
 }
 
@@ -1302,11 +1326,13 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
                   (int)ceil_div(a.vc_len, (int64_t)128), (int)ceil_div(a.N, kRowBlock),
                   a.vc_len, a.D};
   // dead M tiles are zeroed by a plain store kernel first; the GEMM passes them over
-  const cudaError_t zerr = launch_zero_dead_mtiles(a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
+  if (zero_kernel_enabled()) {
+    const cudaError_t zerr = launch_zero_dead_mtiles(a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
                                                    (int)ceil_div(ceil_div(a.N, kRowBlock), 32), a.vc_len,
                                                    a.D * (int64_t)sizeof(T), epi.out, s);
-  if (zerr != cudaSuccess) return zerr;
-  epi.dead_zeroed = 1;
+    if (zerr != cudaSuccess) return zerr;
+    epi.dead_zeroed = 1;
+  }
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;
