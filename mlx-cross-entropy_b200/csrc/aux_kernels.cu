@@ -181,24 +181,6 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
   }
 }
 
-// grad_c rows of a vocabulary chunk's 128-row M tiles that no kept block
-// reaches are zero.  One block per M tile: its row of the transposed mask
-// table (bit = row block) is tested, and a dead tile's rows are written with
-// 16-byte zero stores (rows are whole multiples of 16 bytes).
-__global__ void __launch_bounds__(256)
-zero_dead_mtiles_kernel(const uint32_t* __restrict__ keep_t, int64_t ld, int words, int64_t rows,
-                        int64_t row_bytes, char* __restrict__ out) {
-  const int64_t m = blockIdx.x;
-  int live = 0;
-  for (int w = threadIdx.x; w < words; w += blockDim.x) live |= keep_t[m * ld + w] != 0u;
-  if (__syncthreads_or(live)) return;
-  const int64_t r0 = m * 128;
-  const int64_t r1 = r0 + 128 < rows ? r0 + 128 : rows;
-  uint4* dst = reinterpret_cast<uint4*>(out + r0 * row_bytes);
-  const int64_t n = (r1 - r0) * row_bytes / 16;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = make_uint4(0u, 0u, 0u, 0u);
-}
-
 template <typename T>
 __global__ void cast_f32_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -436,15 +418,6 @@ cudaError_t launch_dequantize(const uint32_t* wq, const void* scales, const void
     case CCE_BF16: return dequant_out<__nv_bfloat16>(wq, scales, biases, rows, D, group, bits, out_dtype, out, stream);
   }
   return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_zero_dead_mtiles(const uint32_t* keep_t, int64_t ld, int words, int64_t rows, int64_t row_bytes,
-                                    void* out, cudaStream_t stream) {
-  const int64_t tiles = ceil_div(rows, 128);
-  if (tiles == 0) return cudaSuccess;
-  zero_dead_mtiles_kernel<<<(unsigned)tiles, 256, 0, stream>>>(keep_t, ld, words, rows, row_bytes,
-                                                               static_cast<char*>(out));
-  return launched();
 }
 
 cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream) {

@@ -80,11 +80,6 @@ cudaError_t launch_sum2_f32(const float* a, const float* b, void* dst, int dtype
 // out[0] = s = the power of two >= max |x| (1 if all zero), out[1] = 1 / s
 cudaError_t launch_pow2_absmax(const float* x, int64_t n, float* out, cudaStream_t stream);
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t stream);
-// Zeroes the rows [128 m, 128 m + 128) of `out` (rows x row_bytes, row_bytes a
-// multiple of 16, out 16-byte aligned) of every 128-row M tile m whose mask
-// table row keep_t[m * ld + 0 .. words) is all zero (grad_c's dead tiles).
-cudaError_t launch_zero_dead_mtiles(const uint32_t* keep_t, int64_t ld, int words, int64_t rows, int64_t row_bytes,
-                                    void* out, cudaStream_t stream);
 
 // ---- SIMT kernels (simt_kernels.cu): any dtype, any shape ----
 cudaError_t simt_forward(const FwdArgs& a, cudaStream_t stream);

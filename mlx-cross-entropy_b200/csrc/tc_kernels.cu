@@ -59,7 +59,6 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t BOX_MN_BYTES = 64 * BK * 2;  // one 64 x 64 MN-major box (8 KB)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int RING = 4;                          // depth of the tile-id ring
-constexpr int kMaxClaim = 16;                    // default most unit ids one scheduler atomic claims
 // Statistics tiles (kStatTile vocabulary columns each, the filter's column
 // granularity) per engine tile and per K-block.
 constexpr int kGroups = BN / kStatTile;                // per 256-column output tile
@@ -573,13 +572,8 @@ struct GradCEpi {
     if (r >= lim) return kb1;
     return max(kb, r * kKpr);
   }
-  // An M tile no K-block reaches (no kept block in its 128 vocabulary rows)
-  // is zeroed beforehand by zero_dead_mtiles when `dead_zeroed` is set: the
-  // producer passes its units over.
-  int dead_zeroed;
-  __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int kb0, int kb1) const {
-    return dead_zeroed && next_kb(mk, mb, nb, kb0, kb1) >= kb1;
-  }
+  // Every tile is written (zero tiles with plain stores, see zero_tile).
+  __device__ __forceinline__ bool skip_unit(const MaskView&, int, int, int, int) const { return false; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ bool zero_shortcut() const { return true; }
   // A tile no K-block reached is zero: lane l stores 8 columns of each row.
@@ -730,28 +724,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      // Work units are claimed from the global counter (dynamic schedule) or
-      // in a fixed stride (static).  The next id is claimed one unit ahead, so
-      // the atomic's latency overlaps the current unit's loads.  A unit the
-      // epilogue has nothing to do for (Epi::skip_unit) is passed over here
-      // and never reaches the MMA and epilogue warps; after a passed-over unit
-      // the next claim takes twice as many ids (up to sched.max_claim), after a live
-      // one a single id, so long runs of dead units cost few atomics while
-      // live units stay balanced across the SMs.
+      // Work units are claimed one id at a time from the global counter
+      // (dynamic schedule) or in a fixed stride (static).  The next id is
+      // claimed one unit ahead, so the atomic's latency overlaps the current
+      // unit's loads.  A unit the epilogue has nothing to do for
+      // (Epi::skip_unit) is passed over here and never reaches the MMA and
+      // epilogue warps.  (Claiming several ids per atomic after dead units
+      // measured slower: live tiles then bunch up on a few SMs.)
       int next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x;
-      int nend = next + 1;  // claimed ids [next, nend)
-      int sidx = 0;         // static schedule: claims made
-      int batch = 1;
-      auto advance = [&](bool skipped) {
-        if (++next < nend) return;
-        if (sched.counter) {
-          batch = skipped ? (batch * 2 < sched.max_claim ? batch * 2 : (sched.max_claim > 1 ? sched.max_claim : 1)) : 1;
-          next = atomicAdd(sched.counter, batch);
-          nend = next + batch;
-        } else {
-          next = (int)blockIdx.x + (++sidx) * (int)gridDim.x;
-          nend = next + 1;
-        }
+      int sidx = 0;  // static schedule: claims made
+      auto advance = [&]() {
+        next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x + (++sidx) * (int)gridDim.x;
       };
       for (int i = 0;; ++i) {
         const int slot = i & (RING - 1);
@@ -763,7 +746,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           sched.coords(u, mb, nb, ks);
           sched.krange(ks, kb0, kb1);
           const bool skip = epi.skip_unit(mk, mb, nb, kb0, kb1);
-          advance(skip);
+          advance();
           if (!skip) {
             tile = u;
             break;
@@ -1068,28 +1051,12 @@ bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int6
   return r == CUDA_SUCCESS;
 }
 
-// A/B switches for timing, read once from the environment:
-// CCE_GRAD_E_HALF_K=0 makes grad_e load whole K-blocks only;
-// CCE_GRAD_C_ZERO_KERNEL=0 leaves grad_c's dead M tiles to the GEMM's
-// epilogue (plain zero stores per tile) instead of a zeroing kernel;
-// CCE_SCHED_MAX_CLAIM=<n> caps the ids one scheduler claim takes (default 16).
-bool env_flag(const char* name, bool dflt) {
-  const char* s = getenv(name);
-  return s == nullptr || s[0] == 0 ? dflt : s[0] != '0';
-}
+// CCE_GRAD_E_HALF_K=0 in the environment makes grad_e load whole K-blocks
+// only (an A/B switch for timing; read once).
 bool half_k_enabled() {
-  static const bool v = env_flag("CCE_GRAD_E_HALF_K", true);
-  return v;
-}
-bool zero_kernel_enabled() {
-  static const bool v = env_flag("CCE_GRAD_C_ZERO_KERNEL", true);
-  return v;
-}
-int max_claim() {
-  static const int v = [] {
-    const char* s = getenv("CCE_SCHED_MAX_CLAIM");
-    const int n = s ? atoi(s) : 0;
-    return n >= 1 && n <= 64 ? n : kMaxClaim;
+  static const bool v = [] {
+    const char* s = getenv("CCE_GRAD_E_HALF_K");
+    return !(s != nullptr && s[0] == '0');
   }();
   return v;
 }
@@ -1191,9 +1158,7 @@ cudaError_t launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const CU
   if (tiles == 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   const uint32_t idesc = instr_desc(BM, BN, bf16, A_MN, B_MN);
-  Sched sc = s;
-  sc.max_claim = max_claim();
-  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmAalt, tmBalt, tmC, sc, epi, idesc);
+  kern<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmB, tmAalt, tmBalt, tmC, s, epi, idesc);
   return launched();
 }
 
@@ -1325,14 +1290,6 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
                   a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
                   (int)ceil_div(a.vc_len, (int64_t)128), (int)ceil_div(a.N, kRowBlock),
                   a.vc_len, a.D};
-  // dead M tiles are zeroed by a plain store kernel first; the GEMM passes them over
-  if (zero_kernel_enabled()) {
-    const cudaError_t zerr = launch_zero_dead_mtiles(a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
-                                                   (int)ceil_div(ceil_div(a.N, kRowBlock), 32), a.vc_len,
-                                                   a.D * (int64_t)sizeof(T), epi.out, s);
-    if (zerr != cudaSuccess) return zerr;
-    epi.dead_zeroed = 1;
-  }
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;
