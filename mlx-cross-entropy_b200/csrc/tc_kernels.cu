@@ -201,6 +201,7 @@ template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
+  static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 0;  // slot in g_mma_cols
   const int32_t* targets;
   const void* bias;
@@ -287,6 +288,7 @@ template <typename T, typename TB>
 struct DlogitsEpi {
   static constexpr bool kNarrowB = true;  // B rows loaded for a tile's live column run only
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
+  static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 1;  // slot in g_mma_cols
   const int32_t* targets;
   const float* lse;
@@ -403,6 +405,7 @@ struct DlogitsEpi {
 struct GradEEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr bool kHalfK = true;  // half K-blocks loaded alone when half_k is set
+  static constexpr bool kWideCapable = true;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 2;  // slot in g_mma_cols
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
   const void* mask_src;     // keep + vc0 / kStatTile: the chunk's columns of the [nRb][nVt] byte mask
@@ -416,6 +419,13 @@ struct GradEEpi {
   peer::Peers peers;
   peer::Layout layout;
   int half_k;               // the half-K maps are valid: load half K-blocks alone
+  // Wide units: a unit is an output tile pair (nb = 2 np, 2 np + 1) of one
+  // K range, accumulated in both 256-column TMEM accumulators at once from
+  // one A stage, K stepping by statistics tile (32 rows: a 128 x 32 A box,
+  // a 32 x 512 B box).  Each unit loads A once for 512 output columns, which
+  // halves the A strips the ~148 units in flight stream from DRAM; the price
+  // is no overlap of a unit's epilogue with the next unit's MMAs.
+  int wide;
 
   struct State {
     int64_t col0;
@@ -454,8 +464,14 @@ struct GradEEpi {
     return m;
   }
   // First K-block in [kb, kb1) with a kept statistics tile in row block mb, else kb1.
+  // (Wide units step by statistics tile: kb is a statistics-tile index.)
   __device__ __forceinline__ int next_kb(const MaskView& mk, int mb, int, int kb, int kb1) const {
     if (mb >= mask_rows) return kb1;
+    if (wide) {
+      const int lim = min(kb1, mask_cols);
+      const int t = mk.next(mb, kb, lim);
+      return t < lim ? t : kb1;
+    }
     const int lim = min(kSpk * kb1, mask_cols);
     const int t = mk.next(mb, kSpk * kb, lim);
     return t < lim ? t / kSpk : kb1;
@@ -541,6 +557,7 @@ template <typename T>
 struct GradCEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
+  static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 3;  // slot in g_mma_cols
   T* out;        // grad_c + vc0 * D
   const float* scale;       // fp16: {s, 1/s}, the products are multiplied by s; else nullptr
@@ -778,6 +795,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
           const int k0 = kb * BK;
+          if constexpr (Epi::kWideCapable) {
+            if (epi.wide) {
+              // one statistics tile of K for the tile pair nb = 2 np, 2 np + 1
+              const int kt = kb * kStatTile;
+              mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + 2 * B_HALF_BYTES);
+              tma_load_2d(a, &tmAalt, full + stage, kt, mb * BM);
+              tma_load_3d(b, &tmBalt, full + stage, 0, kt, nb * (2 * BN / 64));
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
+            }
+          }
           if constexpr (Epi::kHalfK) {
             // one kept statistics tile (ksub_mask 0x3 or 0xC): load that half only
             const uint32_t km = epi.half_k ? epi.ksub_mask(mk, mb, nb, kb) : 0xFu;
@@ -856,6 +887,39 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         sched.coords(tile, mb, nb, ks);
         sched.krange(ks, kb0, kb1);
         if (!epi.tile_active(mk, mb, nb)) continue;
+        if constexpr (Epi::kWideCapable) {
+          if (epi.wide) {
+            // both accumulators: columns [0, 256) for nb = 2 np, [256, 512) for 2 np + 1
+            if (!mbar_wait(tempty + 0, acc_phase ^ 1u, 2) || !mbar_wait(tempty + 1, acc_phase ^ 1u, 2)) break;
+            tc_fence_after();
+            bool ok = true;
+            uint32_t fresh = 1;
+            constexpr uint32_t b_second = (4 * BOX_MN_HALF_BYTES) >> 4;  // slabs 4-7 of the B box
+            for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+              mma_cols += 4ull * BN;
+              if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
+              const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4);
+#pragma unroll
+              for (int k = 0; k < kStatTile / 16; ++k) {
+                mma_f16(tmem_base, ad + k * a_kstep, bd + k * b_kstep, idesc, fresh ^ 1u);
+                mma_f16(tmem_base + BN, ad + k * a_kstep, bd + b_second + k * b_kstep, idesc, fresh ^ 1u);
+                fresh = 0;
+              }
+              mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            mma_commit(tfull + 0);
+            mma_commit(tfull + 1);
+            acc_phase ^= 1u;
+            continue;
+          }
+        }
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -948,39 +1012,61 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         epi.inactive_tile(mb, nb, r);
         continue;
       }
-      if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
-      tc_fence_after();
       const bool any_kb = !Epi::kMask || epi.next_kb(mk, mb, nb, kb0, kb1) < kb1;
-      typename Epi::State st;
-      epi.begin(st, mk, mb, nb, r, ks);
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      // a tile no K-block reached is all zeros: plain coalesced zero stores
-      // (or nothing, when zeros would be added), not the staged path
-      bool zero_tile = false;
-      if constexpr (Epi::kZeroTiles) zero_tile = !any_kb && epi.zero_shortcut();
-      if (zero_tile) {
-        if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
-      } else {
-        // the TMEM load of chunk c + 1 is in flight while chunk c is processed
-        uint32_t cur[32], nxt[32];
-        bool cur_live = any_kb && epi.chunk_live(st, 0);
-        if (cur_live) tmem_ld32_issue(tbase, cur);
+      // One output tile from the accumulator at column `col`.
+      auto drain_tile = [&](int nbt, uint32_t col) {
+        typename Epi::State st;
+        epi.begin(st, mk, mb, nbt, r, ks);
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + col;
+        // a tile no K-block reached is all zeros: plain coalesced zero stores
+        // (or nothing, when zeros would be added), not the staged path
+        bool zero_tile = false;
+        if constexpr (Epi::kZeroTiles) zero_tile = !any_kb && epi.zero_shortcut();
+        if (zero_tile) {
+          if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
+        } else {
+          // the TMEM load of chunk c + 1 is in flight while chunk c is processed
+          uint32_t cur[32], nxt[32];
+          bool cur_live = any_kb && epi.chunk_live(st, 0);
+          if (cur_live) tmem_ld32_issue(tbase, cur);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          __syncwarp();
-          const bool nxt_live = c + 1 < BN / 32 && any_kb && epi.chunk_live(st, c + 1);
-          if (cur_live) tmem_ld_wait(cur);
-          if (nxt_live) tmem_ld32_issue(tbase + (c + 1) * 32, nxt);
-          float v[32];
+          for (int c = 0; c < BN / 32; ++c) {
+            __syncwarp();
+            const bool nxt_live = c + 1 < BN / 32 && any_kb && epi.chunk_live(st, c + 1);
+            if (cur_live) tmem_ld_wait(cur);
+            if (nxt_live) tmem_ld32_issue(tbase + (c + 1) * 32, nxt);
+            float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = cur_live ? __uint_as_float(cur[j]) : 0.f;
-          epi.chunk(st, c, v, sg);
+            for (int j = 0; j < 32; ++j) v[j] = cur_live ? __uint_as_float(cur[j]) : 0.f;
+            epi.chunk(st, c, v, sg);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
-          cur_live = nxt_live;
+            for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+            cur_live = nxt_live;
+          }
+        }
+        epi.end(st);
+      };
+      if constexpr (Epi::kWideCapable) {
+        if (epi.wide) {
+          // the tile pair 2 nb, 2 nb + 1 from accumulators 0 and 1
+          bool ok = true;
+          for (int h = 0; h < 2; ++h) {
+            if (!mbar_wait(tfull + h, acc_phase, 4)) { ok = false; break; }
+            tc_fence_after();
+            if ((int64_t)(2 * nb + h) * BN < epi.D) drain_tile(2 * nb + h, (uint32_t)(h * BN));
+            __syncwarp();
+            tc_fence_before();
+            mbar_arrive(tempty + h);
+          }
+          if (!ok) break;
+          epi.after_unit(ubar, uphase);
+          acc_phase ^= 1u;
+          continue;
         }
       }
-      epi.end(st);
+      if (!mbar_wait(tfull + acc, acc_phase, 4)) break;
+      tc_fence_after();
+      drain_tile(nb, (uint32_t)(acc * BN));
       epi.after_unit(ubar, uphase);
       __syncwarp();
       tc_fence_before();
@@ -1051,12 +1137,21 @@ bool make_tmap(CUtensorMap* tm, const void* base, bool bf16, int64_t inner, int6
   return r == CUDA_SUCCESS;
 }
 
-// CCE_GRAD_E_HALF_K=0 in the environment makes grad_e load whole K-blocks
-// only (an A/B switch for timing; read once).
+// A/B switches for timing, read once from the environment:
+// CCE_GRAD_E_WIDE=0 runs grad_e as single 128 x 256 tiles (64-row K-blocks)
+// instead of wide units; CCE_GRAD_E_HALF_K=0 then loads whole K-blocks only.
+bool env_on(const char* name) {
+  const char* s = getenv(name);
+  return !(s != nullptr && s[0] == '0');
+}
 bool half_k_enabled() {
+  static const bool v = env_on("CCE_GRAD_E_HALF_K");
+  return v;
+}
+bool wide_enabled() {
   static const bool v = [] {
-    const char* s = getenv("CCE_GRAD_E_HALF_K");
-    return !(s != nullptr && s[0] == '0');
+    const char* s = getenv("CCE_GRAD_E_WIDE");
+    return s != nullptr && s[0] == '1';
   }();
   return v;
 }
@@ -1267,13 +1362,22 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
     epi.peers = push->peers;
     epi.layout = push->layout;
   }
-  // half K-block boxes: A (dlogits) 32 columns wide in the 64-byte swizzle,
-  // B (the c chunk) 32 rows of the 3-D MN-major form
+  // A (dlogits) in boxes 32 columns wide in the 64-byte swizzle, and B (the
+  // c chunk) in boxes of 32 rows of the 3-D MN-major form: 512 columns for
+  // wide units, 256 for half K-blocks
   CUtensorMap tmAh = tmA, tmBh = tmB;
-  epi.half_k = (b3d && half_k_enabled() &&
-                make_tmap(&tmAh, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
-                make_tmap_mn3d(&tmBh, cchunk, bf16, a.D, a.vc_len, a.D, BK / 2, BN / 64))
-                   ? 1 : 0;
+  const bool a_half = b3d && make_tmap(&tmAh, a.dlogits, bf16, a.vc_len, a.N, a.vc_ld, BK / 2, BM,
+                                       CU_TENSOR_MAP_SWIZZLE_64B);
+  if (a_half && wide_enabled() && make_tmap_mn3d(&tmBh, cchunk, bf16, a.D, a.vc_len, a.D, kStatTile, 2 * BN / 64)) {
+    epi.wide = 1;
+    sc.num_n = (int)ceil_div(ceil_div(a.D, BN), 2);
+    sc.num_kb = (int)ceil_div(a.vc_len, kStatTile);
+    if (push != nullptr) epi.total_units = (unsigned)sc.units();
+  } else {
+    epi.half_k = (a_half && half_k_enabled() &&
+                  make_tmap_mn3d(&tmBh, cchunk, bf16, a.D, a.vc_len, a.D, BK / 2, BN / 64))
+                     ? 1 : 0;
+  }
   return launch_gemm<false, true>(tmA, tmB, tmAh, tmBh, tmC, sc, epi, bf16, s);
 }
 
