@@ -1149,10 +1149,7 @@ bool half_k_enabled() {
   return v;
 }
 bool wide_enabled() {
-  static const bool v = [] {
-    const char* s = getenv("CCE_GRAD_E_WIDE");
-    return s != nullptr && s[0] == '1';
-  }();
+  static const bool v = env_on("CCE_GRAD_E_WIDE");
   return v;
 }
 
