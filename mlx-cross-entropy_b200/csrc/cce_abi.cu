@@ -82,17 +82,20 @@ constexpr size_t kAlign = 256;
 // dlogits chunk buffer: aim for 32768 vocabulary rows per chunk within 128 MiB
 // to 1 GiB of buffer.  Every chunk costs three kernel launches whatever its
 // work (~70 us at N = 2048 when the filter rejects nearly every block), so
-// smaller N may grow its chunks up to 256 MiB of buffer, but never past half
+// N below 4096 grows its chunks up to 512 MiB of buffer, but never past half
 // of the vocabulary: the buffer stays below half of the [N, V] logits, the
 // memory bound of the whole method.  Measured on B200: config 3 (N = 4096)
 // backward 8.71 ms at 16384 rows, 8.35 at 32768, 8.42 at 65536, 8.62 at
-// 131072; config 4 (N = 2048) 1.44 ms in 8 chunks, 1.15 in 4, 1.01 in 2;
-// config 2 (N = 1024) 0.65 ms in 2 chunks.  (Two buffers, so that a chunk's
-// dlogits overlap the previous chunk's grads, measured no faster.)
+// 131072 (and, with the current grad_e, whole steps equal at 32768 and
+// 65536 rows); config 4 (N = 2048) 1.44 ms in 8 chunks, 1.15 in 4, 1.01 in 2
+// (whole steps 2.76 ms in 4 chunks, 2.63 in 2); config 2 (N = 1024) in 2
+// chunks.  (Two buffers, so that a chunk's dlogits overlap the previous
+// chunk's grads, measured no faster.)
 constexpr int64_t kDlTargetRows = 32768;
 constexpr int64_t kDlMaxBytes = 1ll << 30;
 constexpr int64_t kDlMinBytes = 128ll << 20;
-constexpr int64_t kDlSmallNBytes = 256ll << 20;
+constexpr int64_t kDlSmallNBytes = 256ll << 20;  // N below this many bytes per 32768 rows is "small"
+constexpr int64_t kDlSmallNGrowBytes = 512ll << 20;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -158,9 +161,9 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   int64_t vc = (budget / (nrow * elt)) / gran * gran;
   if (vc < gran) vc = gran;
   if (target == kDlTargetRows && nrow * 2 * target < kDlSmallNBytes) {
-    // small N: longer chunks, up to 256 MiB and half the vocabulary
+    // small N: longer chunks, up to 512 MiB and half the vocabulary
     const int64_t half = cce::round_up(cce::ceil_div(V > 0 ? V : 1, 2), gran);
-    int64_t grow = (kDlSmallNBytes / (nrow * elt)) / gran * gran;
+    int64_t grow = (kDlSmallNGrowBytes / (nrow * elt)) / gran * gran;
     if (grow > half) grow = half;
     if (grow > vc) vc = grow;
   }
