@@ -524,7 +524,10 @@ int cce_forward(const void* e, const void* c, const void* bias, int bias_dtype,
 }
 
 // Rows of a quantised head expanded per forward chunk (two buffers).
-constexpr int64_t kFwdQuantChunkRows = 16384;
+#ifndef CCE_FWDQ_ROWS
+#define CCE_FWDQ_ROWS 16384
+#endif
+constexpr int64_t kFwdQuantChunkRows = CCE_FWDQ_ROWS;
 
 static size_t forward_q_ws_bytes(int64_t N, int64_t D, int64_t V, int dtype) {
   const int64_t rows = V < kFwdQuantChunkRows ? (V > 0 ? V : 1) : kFwdQuantChunkRows;
