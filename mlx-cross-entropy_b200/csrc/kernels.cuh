@@ -87,8 +87,13 @@ cudaError_t simt_forward(const FwdArgs& a, cudaStream_t stream);
 constexpr int64_t kSimtLseTile = 128;
 constexpr int64_t kTcLseTile = 256;
 cudaError_t simt_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
-// grad_e_acc[N, D] (+)= dl[N, vc_len] @ c[v_offset-local rows vc0.., D]
-cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, cudaStream_t stream);
+// grad_e_acc[N, D] (+)= dl[N, vc_len] @ c[v_offset-local rows vc0.., D]; with
+// splits > 1 the K range is split over that many partial slabs part[splits][N][D]
+// (workspace), summed in split order
+cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, float* part, int splits,
+                        cudaStream_t stream);
+// K splits simt_grad_e uses for an N x D output over chunks of vc rows
+int simt_grad_e_splits(int64_t N, int64_t D, int64_t vc);
 // grad_c[vc0 .. vc0+vc_len, D] = dl^T @ e, written in dtype
 cudaError_t simt_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t stream);
 

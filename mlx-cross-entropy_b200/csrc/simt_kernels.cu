@@ -229,38 +229,42 @@ simt_dlogits_kernel(const T* __restrict__ e, const T* __restrict__ c, const void
 
 // Generic SIMT GEMM: out[m, n] (+)= sum_k A(m, k) * B(k, n), fp32 accumulate.
 //   A(m, k) = A[m * a_sm + k * a_sk] (fp32), B(k, n) = B[k * b_sk + n * b_sn] (TB)
-// A_M_CONTIG selects the coalesced load mapping for A.
+// A_M_CONTIG selects the coalesced load mapping for A.  Split K: block z
+// covers k in [z * k_per, (z + 1) * k_per) and writes out + z * out_z.
 constexpr int GM = 64, GN = 64, GK = 16;
 
 template <typename TB, typename TO, bool A_M_CONTIG>
 __global__ void __launch_bounds__(THREADS)
 simt_gemm_kernel(const float* __restrict__ A, int64_t a_sm, int64_t a_sk, const TB* __restrict__ B,
                  int64_t b_sk, int64_t b_sn, int64_t M, int64_t Nn, int64_t K, TO* __restrict__ out,
-                 int64_t ld_out, bool accumulate) {
+                 int64_t ld_out, bool accumulate, int64_t k_per, int64_t out_z) {
   __shared__ float As[GK][GM + 4];
   __shared__ float Bs[GK][GN + 4];
   const int64_t m0 = (int64_t)blockIdx.y * GM, n0 = (int64_t)blockIdx.x * GN;
+  const int64_t kbeg = (int64_t)blockIdx.z * k_per;
+  const int64_t kend = kbeg + k_per < K ? kbeg + k_per : K;
+  out += (int64_t)blockIdx.z * out_z;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  for (int64_t k0 = 0; k0 < K; k0 += GK) {
+  for (int64_t k0 = kbeg; k0 < kend; k0 += GK) {
 #pragma unroll
     for (int it = 0; it < (GM * GK) / THREADS; ++it) {
       const int idx = threadIdx.x + it * THREADS;
       int m, k;
       if (A_M_CONTIG) { m = idx % GM; k = idx / GM; } else { k = idx % GK; m = idx / GK; }
       const int64_t gm = m0 + m, gk = k0 + k;
-      As[k][m] = (gm < M && gk < K) ? A[gm * a_sm + gk * a_sk] : 0.f;
+      As[k][m] = (gm < M && gk < kend) ? A[gm * a_sm + gk * a_sk] : 0.f;
     }
 #pragma unroll
     for (int it = 0; it < (GN * GK) / THREADS; ++it) {
       const int idx = threadIdx.x + it * THREADS;
       const int n = idx % GN, k = idx / GN;
       const int64_t gn = n0 + n, gk = k0 + k;
-      Bs[k][n] = (gn < Nn && gk < K) ? to_f32(B[gk * b_sk + gn * b_sn]) : 0.f;
+      Bs[k][n] = (gn < Nn && gk < kend) ? to_f32(B[gk * b_sk + gn * b_sn]) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -289,6 +293,17 @@ simt_gemm_kernel(const float* __restrict__ A, int64_t a_sm, int64_t a_sk, const 
       if (accumulate) v += to_f32(out[m * ld_out + n]);
       out[m * ld_out + n] = from_f32<TO>(v);
     }
+  }
+}
+
+// acc[i] = (accumulate ? acc[i] : 0) + part[0][i] + part[1][i] + ... in that
+// order: the split-K partials summed deterministically.
+__global__ void sum_splits_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ acc,
+                                  bool accumulate) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = accumulate ? acc[i] : 0.f;
+    for (int z = 0; z < splits; ++z) v += part[(int64_t)z * n + i];
+    acc[i] = v;
   }
 }
 
@@ -358,15 +373,33 @@ cudaError_t simt_dlogits(const BwdChunkArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, cudaStream_t s) {
+int simt_grad_e_splits(int64_t N, int64_t D, int64_t vc) {
+  // enough blocks for two waves of 148 SMs, at most 8 splits of >= 1024 rows
+  const int64_t tiles = ceil_div(N, GM) * ceil_div(D, GN);
+  int64_t sp = ceil_div(2 * 148, tiles > 0 ? tiles : 1);
+  if (sp > 8) sp = 8;
+  if (sp > vc / 1024) sp = vc / 1024;
+  return sp < 1 ? 1 : (int)sp;
+}
+
+cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulate, float* part, int splits,
+                        cudaStream_t s) {
   if (a.N == 0 || a.D == 0) return cudaSuccess;
   // A(m = row, k = v) = dl[row * ld + v]; B(k = v, n = d) = c_chunk[v * D + d] (row vc0 + v of c)
-  dim3 grid((unsigned)ceil_div(a.D, GN), (unsigned)ceil_div(a.N, GM));
+  // Few output tiles (small N x D) leave most SMs idle over a long K: the K
+  // range is then split over `splits` blocks per tile writing partials that
+  // sum_splits_kernel adds in split order.
+  const bool split = splits > 1 && part != nullptr;
+  const int sp = split ? splits : 1;
+  const int64_t k_per = split ? ceil_div(ceil_div(a.vc_len, sp), GK) * GK : a.vc_len;
+  dim3 grid((unsigned)ceil_div(a.D, GN), (unsigned)ceil_div(a.N, GM), (unsigned)sp);
   const float* dl = (const float*)a.dlogits;
+  float* out = split ? part : grad_e_acc;
+  const bool acc_in = split ? false : accumulate;
+  const int64_t out_z = a.N * a.D;
 #define CCE_GE_LAUNCH(T)                                                                       \
   simt_gemm_kernel<T, float, false><<<grid, THREADS, 0, s>>>(                                  \
-      dl, a.vc_ld, 1, (const T*)a.c_chunk, a.D, 1, a.N, a.D, a.vc_len, grad_e_acc, a.D, \
-      accumulate)
+      dl, a.vc_ld, 1, (const T*)a.c_chunk, a.D, 1, a.N, a.D, a.vc_len, out, a.D, acc_in, k_per, out_z)
   switch (a.dtype) {
     case CCE_F32: CCE_GE_LAUNCH(float); break;
     case CCE_F16: CCE_GE_LAUNCH(__half); break;
@@ -374,6 +407,12 @@ cudaError_t simt_grad_e(const BwdChunkArgs& a, float* grad_e_acc, bool accumulat
     default: return cudaErrorInvalidValue;
   }
 #undef CCE_GE_LAUNCH
+  cudaError_t err = launched();
+  if (err != cudaSuccess || !split) return err;
+  const int64_t n = a.N * a.D;
+  int64_t blocks = ceil_div(n, 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  sum_splits_kernel<<<(unsigned)blocks, 256, 0, s>>>(part, sp, n, grad_e_acc, accumulate);
   return launched();
 }
 
@@ -385,7 +424,7 @@ cudaError_t simt_grad_c(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
 #define CCE_GC_LAUNCH(T)                                                                     \
   simt_gemm_kernel<T, T, true><<<grid, THREADS, 0, s>>>(dl, 1, a.vc_ld, (const T*)a.e, a.D, 1, \
                                                         a.vc_len, a.D, a.N,                    \
-                                                        (T*)grad_c + a.vc0 * a.D, a.D, false)
+                                                        (T*)grad_c + a.vc0 * a.D, a.D, false, a.N, 0)
   switch (a.dtype) {
     case CCE_F32: CCE_GC_LAUNCH(float); break;
     case CCE_F16: CCE_GC_LAUNCH(__half); break;

@@ -88,7 +88,7 @@ def test_quantized_cce_matches_dense_and_oracle(reduction, monkeypatch):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_quantized_head_several_forward_chunks(dtype, monkeypatch):
-    """V = 40000 spans three 16384-row forward chunks (the last one ragged)
+    """V = 40000 spans two 32768-row forward chunks (the last one ragged)
     and five 8192-row backward chunks; bf16 runs on the tensor cores, float32
     on the CUDA cores.  Against the dense path on the same dequantised head."""
     monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "8192")
