@@ -131,19 +131,26 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
   constexpr int kTilesPerWarp = kMaskTiles / kMaskWarps;
   int skipped = 0, total = 0;
   const int64_t tile0 = (int64_t)blockIdx.x * kMaskRounds * kMaskTiles;
-#pragma unroll 1
-  for (int r = 0; r < kMaskRounds; ++r) {
+  // All of this warp's tile maxima of a round are loaded before any is
+  // tested, and the next round's are loaded before this round's are tested,
+  // so two rounds of loads are in flight at a time.
+  float x[kTilesPerWarp][kRowsPerLane], xn[kTilesPerWarp][kRowsPerLane];
+  auto load_round = [&](int r, float (&dst)[kTilesPerWarp][kRowsPerLane]) {
     const int64_t base = tile0 + (int64_t)r * kMaskTiles;
-    if (base >= nVt) break;
-    // all of this warp's tile maxima of the round are loaded before any is
-    // tested, so the loads overlap
-    float x[kTilesPerWarp][kRowsPerLane];
 #pragma unroll
     for (int q = 0; q < kTilesPerWarp; ++q) {
       const int64_t j = base + warp + q * kMaskWarps;
 #pragma unroll
-      for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = (live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
+      for (int u = 0; u < kRowsPerLane; ++u)
+        dst[q][u] = (r < kMaskRounds && live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
     }
+  };
+  load_round(0, x);
+#pragma unroll 1
+  for (int r = 0; r < kMaskRounds; ++r) {
+    const int64_t base = tile0 + (int64_t)r * kMaskTiles;
+    if (base >= nVt) break;
+    load_round(r + 1, xn);
 #pragma unroll
     for (int q = 0; q < kTilesPerWarp; ++q) {
       const int w = warp + q * kMaskWarps;
@@ -165,6 +172,10 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
       ++total;
       skipped += k ? 0 : 1;
     }
+#pragma unroll
+    for (int q = 0; q < kTilesPerWarp; ++q)
+#pragma unroll
+      for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = xn[q][u];
   }
   if (skip_stats && lane == 0 && total) {
     atomicAdd(&cnt[0], skipped);
