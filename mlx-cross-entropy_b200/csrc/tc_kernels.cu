@@ -221,7 +221,6 @@ struct FwdEpi {
   static constexpr bool kZeroTiles = false;
   __device__ __forceinline__ bool tile_active(const MaskView&, int, int) const { return true; }
   __device__ __forceinline__ bool skip_unit(const MaskView&, int, int, int, int) const { return false; }
-  __device__ __forceinline__ int k_start(int, int kb0, int, int) const { return kb0; }
   __device__ __forceinline__ uint32_t col_mask(const MaskView&, int, int) const { return kAllGroups; }
   __device__ __forceinline__ int next_kb(const MaskView&, int, int, int kb, int) const { return kb; }
   __device__ __forceinline__ uint32_t ksub_mask(const MaskView&, int, int, int) const { return 0xFu; }
@@ -324,7 +323,6 @@ struct DlogitsEpi {
   __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int, int) const {
     return !tile_active(mk, mb, nb);
   }
-  __device__ __forceinline__ int k_start(int, int kb0, int, int) const { return kb0; }
   // Column groups the MMA computes: only the kept ones (the epilogue never
   // reads the accumulator columns of the others).
   __device__ __forceinline__ uint32_t col_mask(const MaskView& mk, int mb, int nb) const {
@@ -484,15 +482,6 @@ struct GradEEpi {
   __device__ __forceinline__ bool skip_unit(const MaskView& mk, int mb, int nb, int kb0, int kb1) const {
     return accumulate && !push && next_kb(mk, mb, nb, kb0, kb1) >= kb1;
   }
-  // Wide units with `rotate` start their K range at an offset that grows with
-  // the unit's place in the wave (unit id mod grid): units claimed in order
-  // then stand at about the same K position of their ranges at any moment,
-  // so the A and B blocks they share are fetched from DRAM once per wave.
-  int rotate;
-  __device__ __forceinline__ int k_start(int unit, int kb0, int kb1, int grid) const {
-    if (!wide || !rotate || grid <= 0) return kb0;
-    return kb0 + (int)(((long long)(unit % grid) * (kb1 - kb0)) / grid);
-  }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   template <class S>
   __device__ __forceinline__ bool chunk_live(const S&, int) const { return true; }
@@ -602,7 +591,6 @@ struct GradCEpi {
   }
   // Every tile is written (zero tiles with plain stores, see zero_tile).
   __device__ __forceinline__ bool skip_unit(const MaskView&, int, int, int, int) const { return false; }
-  __device__ __forceinline__ int k_start(int, int kb0, int, int) const { return kb0; }
   __device__ __forceinline__ void inactive_tile(int, int, int) const {}
   __device__ __forceinline__ bool zero_shortcut() const { return true; }
   // A tile no K-block reached is zero: lane l stores 8 columns of each row.
@@ -802,72 +790,68 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         const uint32_t tx_bytes = A_BYTES + (nn0 < (uint32_t)kGroups ? nn0 * B32_BYTES : B_BYTES);
         bool ok = true;
-        // K-blocks [kr, kb1) then [kb0, kr): kr = kb0 unless the epilogue rotates the range
-        for (int seg = 0, kr = epi.k_start(tile, kb0, kb1, (int)gridDim.x); seg < 2 && ok; ++seg) {
-          const int klo = seg ? kb0 : kr, khi = seg ? kr : kb1;
-          for (int kb = epi.next_kb(mk, mb, nb, klo, khi); kb < khi; kb = epi.next_kb(mk, mb, nb, kb + 1, khi)) {
-            if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
-            uint8_t* a = sA + stage * A_BYTES;
-            uint8_t* b = sB + stage * B_BYTES;
-            const int k0 = kb * BK;
-            if constexpr (Epi::kWideCapable) {
-              if (epi.wide) {
-                // one statistics tile of K for the tile pair nb = 2 np, 2 np + 1
-                const int kt = kb * kStatTile;
-                mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + 2 * B_HALF_BYTES);
-                tma_load_2d(a, &tmAalt, full + stage, kt, mb * BM);
-                tma_load_3d(b, &tmBalt, full + stage, 0, kt, nb * (2 * BN / 64));
-                if (++stage == STAGES) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
-                continue;
+        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+          if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
+          uint8_t* a = sA + stage * A_BYTES;
+          uint8_t* b = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if constexpr (Epi::kWideCapable) {
+            if (epi.wide) {
+              // one statistics tile of K for the tile pair nb = 2 np, 2 np + 1
+              const int kt = kb * kStatTile;
+              mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + 2 * B_HALF_BYTES);
+              tma_load_2d(a, &tmAalt, full + stage, kt, mb * BM);
+              tma_load_3d(b, &tmBalt, full + stage, 0, kt, nb * (2 * BN / 64));
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
               }
+              continue;
             }
-            if constexpr (Epi::kHalfK) {
-              // one kept statistics tile (ksub_mask 0x3 or 0xC): load that half only
-              const uint32_t km = epi.half_k ? epi.ksub_mask(mk, mb, nb, kb) : 0xFu;
-              if (km != 0xFu) {
-                const int kh = k0 + (km == 0x3u ? 0 : BK / 2);
-                mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + B_HALF_BYTES);
-                tma_load_2d(a, &tmAalt, full + stage, kh, mb * BM);
-                tma_load_3d(b, &tmBalt, full + stage, 0, kh, nb * (BN / 64));
-                if (++stage == STAGES) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
-                continue;
+          }
+          if constexpr (Epi::kHalfK) {
+            // one kept statistics tile (ksub_mask 0x3 or 0xC): load that half only
+            const uint32_t km = epi.half_k ? epi.ksub_mask(mk, mb, nb, kb) : 0xFu;
+            if (km != 0xFu) {
+              const int kh = k0 + (km == 0x3u ? 0 : BK / 2);
+              mbar_arrive_expect_tx(full + stage, A_HALF_BYTES + B_HALF_BYTES);
+              tma_load_2d(a, &tmAalt, full + stage, kh, mb * BM);
+              tma_load_3d(b, &tmBalt, full + stage, 0, kh, nb * (BN / 64));
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
               }
+              continue;
             }
-            mbar_arrive_expect_tx(full + stage, tx_bytes);
-            if (A_MN) {
-              if (sched.a3d) {
-                tma_load_3d(a, &tmA, full + stage, 0, k0, mb * (BM / 64));
-              } else {
-                tma_load_2d(a, &tmA, full + stage, mb * BM, k0);
-                tma_load_2d(a + BOX_MN_BYTES, &tmA, full + stage, mb * BM + 64, k0);
-              }
+          }
+          mbar_arrive_expect_tx(full + stage, tx_bytes);
+          if (A_MN) {
+            if (sched.a3d) {
+              tma_load_3d(a, &tmA, full + stage, 0, k0, mb * (BM / 64));
             } else {
-              tma_load_2d(a, &tmA, full + stage, k0, mb * BM);
+              tma_load_2d(a, &tmA, full + stage, mb * BM, k0);
+              tma_load_2d(a + BOX_MN_BYTES, &tmA, full + stage, mb * BM + 64, k0);
             }
-            if (B_MN) {
-              if (sched.b3d) {
-                tma_load_3d(b, &tmB, full + stage, 0, k0, nb * (BN / 64));
-              } else {
+          } else {
+            tma_load_2d(a, &tmA, full + stage, k0, mb * BM);
+          }
+          if (B_MN) {
+            if (sched.b3d) {
+              tma_load_3d(b, &tmB, full + stage, 0, k0, nb * (BN / 64));
+            } else {
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
-                  tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
-              }
-            } else if (nn0 < (uint32_t)kGroups) {
-              for (uint32_t g = nj0; g < nj0 + nn0; ++g)
-                tma_load_2d(b + g * B32_BYTES, &tmBalt, full + stage, k0, nb * BN + (int)(g * kStatTile));
-            } else {
-              tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(b + j * BOX_MN_BYTES, &tmB, full + stage, nb * BN + j * 64, k0);
             }
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1u;
-            }
+          } else if (nn0 < (uint32_t)kGroups) {
+            for (uint32_t g = nj0; g < nj0 + nn0; ++g)
+              tma_load_2d(b + g * B32_BYTES, &tmBalt, full + stage, k0, nb * BN + (int)(g * kStatTile));
+          } else {
+            tma_load_2d(b, &tmB, full + stage, k0, nb * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
         if (!ok) break;
@@ -911,26 +895,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             bool ok = true;
             uint32_t fresh = 1;
             constexpr uint32_t b_second = (4 * BOX_MN_HALF_BYTES) >> 4;  // slabs 4-7 of the B box
-            // K-blocks [kr, kb1) then [kb0, kr): kr = kb0 unless the epilogue rotates the range
-            for (int seg = 0, kr = epi.k_start(tile, kb0, kb1, (int)gridDim.x); seg < 2 && ok; ++seg) {
-              const int klo = seg ? kb0 : kr, khi = seg ? kr : kb1;
-              for (int kb = epi.next_kb(mk, mb, nb, klo, khi); kb < khi; kb = epi.next_kb(mk, mb, nb, kb + 1, khi)) {
-                mma_cols += 4ull * BN;
-                if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
-                tc_fence_after();
-                const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
-                const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4);
+            for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+              mma_cols += 4ull * BN;
+              if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
+              const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4);
 #pragma unroll
-                for (int k = 0; k < kStatTile / 16; ++k) {
-                  mma_f16(tmem_base, ad + k * a_kstep, bd + k * b_kstep, idesc, fresh ^ 1u);
-                  mma_f16(tmem_base + BN, ad + k * a_kstep, bd + b_second + k * b_kstep, idesc, fresh ^ 1u);
-                  fresh = 0;
-                }
-                mma_commit(empty + stage);
-                if (++stage == STAGES) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
+              for (int k = 0; k < kStatTile / 16; ++k) {
+                mma_f16(tmem_base, ad + k * a_kstep, bd + k * b_kstep, idesc, fresh ^ 1u);
+                mma_f16(tmem_base + BN, ad + k * a_kstep, bd + b_second + k * b_kstep, idesc, fresh ^ 1u);
+                fresh = 0;
+              }
+              mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
               }
             }
             if (!ok) break;
@@ -965,46 +945,42 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t boff = (kStatTile * 128u * j0) >> 4;
         bool ok = true;
         uint32_t fresh = 1;  // the tile's first MMA overwrites the accumulator
-        // K-blocks [kr, kb1) then [kb0, kr): kr = kb0 unless the epilogue rotates the range
-        for (int seg = 0, kr = epi.k_start(tile, kb0, kb1, (int)gridDim.x); seg < 2 && ok; ++seg) {
-          const int klo = seg ? kb0 : kr, khi = seg ? kr : kb1;
-          for (int kb = epi.next_kb(mk, mb, nb, klo, khi); kb < khi; kb = epi.next_kb(mk, mb, nb, kb + 1, khi)) {
-            const uint32_t km = epi.ksub_mask(mk, mb, nb, kb);  // K=16 steps to issue
-            mma_cols += (unsigned long long)(__popc(km & 0xFu) * kStatTile * n0);
-            if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
-            tc_fence_after();
-            if constexpr (Epi::kHalfK) {
-              if (epi.half_k && km != 0xFu) {
-                // the stage holds the kept half: its two K=16 steps
-                const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
-                const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4) + boff;
+        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+          const uint32_t km = epi.ksub_mask(mk, mb, nb, kb);  // K=16 steps to issue
+          mma_cols += (unsigned long long)(__popc(km & 0xFu) * kStatTile * n0);
+          if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+          tc_fence_after();
+          if constexpr (Epi::kHalfK) {
+            if (epi.half_k && km != 0xFu) {
+              // the stage holds the kept half: its two K=16 steps
+              const uint64_t ad = adesc_h + (uint64_t)((stage * A_BYTES) >> 4);
+              const uint64_t bd = bdesc_h + (uint64_t)((stage * B_BYTES) >> 4) + boff;
 #pragma unroll
-                for (int k = 0; k < BK / 32; ++k) {
-                  mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
-                  fresh = 0;
-                }
-                mma_commit(empty + stage);
-                if (++stage == STAGES) {
-                  stage = 0;
-                  phase ^= 1u;
-                }
-                continue;
-              }
-            }
-            const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
-            const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4) + boff;
-#pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              if ((km >> k) & 1u) {
+              for (int k = 0; k < BK / 32; ++k) {
                 mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
                 fresh = 0;
               }
+              mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
             }
-            mma_commit(empty + stage);
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1u;
+          }
+          const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
+          const uint64_t bd = bdesc0 + (uint64_t)((stage * B_BYTES) >> 4) + boff;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            if ((km >> k) & 1u) {
+              mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
+              fresh = 0;
             }
+          }
+          mma_commit(empty + stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
         if (!ok) break;
@@ -1174,11 +1150,6 @@ bool half_k_enabled() {
 }
 bool wide_enabled() {
   static const bool v = env_on("CCE_GRAD_E_WIDE");
-  return v;
-}
-// CCE_GRAD_E_ROTATE=0: wide units walk their K ranges from the start.
-bool rotate_enabled() {
-  static const bool v = env_on("CCE_GRAD_E_ROTATE");
   return v;
 }
 
@@ -1396,7 +1367,6 @@ cudaError_t grad_e_launch(const BwdChunkArgs& a, float* acc2, bool accumulate, c
                                        CU_TENSOR_MAP_SWIZZLE_64B);
   if (a_half && wide_enabled() && make_tmap_mn3d(&tmBh, cchunk, bf16, a.D, a.vc_len, a.D, kStatTile, 2 * BN / 64)) {
     epi.wide = 1;
-    epi.rotate = rotate_enabled() ? 1 : 0;
     sc.num_n = (int)ceil_div(ceil_div(a.D, BN), 2);
     sc.num_kb = (int)ceil_div(a.vc_len, kStatTile);
     if (push != nullptr) epi.total_units = (unsigned)sc.units();
