@@ -24,6 +24,7 @@ struct Sched {
   int* counter;  // dynamic scheduling: next tile id (zeroed before the launch); nullptr = static
   int group;     // grouped raster: blocks of the fast dimension per group (<= 0: all)
   int ksplit;    // K splits per output tile (<= 1: none); split s is its own work unit
+  int span;      // K-major B: one MMA over the span of a tile's kept column groups
   __host__ __device__ __forceinline__ int splits() const { return ksplit > 1 ? ksplit : 1; }
   __host__ __device__ __forceinline__ int units() const { return num_m * num_n * splits(); }
   // Unit id -> (mb, nb, ks).  All units of split 0 come first, then split 1, ...

@@ -923,17 +923,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        // The tile's statistics-tile column groups to compute: when they form
-        // one run of consecutive groups (j0, n0), one MMA of N = kStatTile n0
-        // columns at B rows kStatTile j0 (K-major B: 128 bytes per row); else
-        // the whole tile.  (Two runs as two MMAs re-read A from shared memory
-        // and measured slower.)
+        // The tile's statistics-tile column groups to compute: the span from
+        // the first to the last kept group (j0, n0) -- one MMA of N =
+        // kStatTile n0 columns at B rows kStatTile j0 (K-major B: 128 bytes
+        // per row); the columns of rejected groups inside the span are
+        // computed and never read.  (Two runs as two MMAs re-read A from
+        // shared memory and measured slower.)  sched.span = 0 narrows only a
+        // single run of kept groups.
         uint32_t j0 = 0, n0 = kGroups;
         if constexpr (!B_MN) {
           const uint32_t cm = epi.col_mask(mk, mb, nb);
-          if (cm != kAllGroups) {
+          if (cm != kAllGroups && cm != 0u) {
             const uint32_t j = __ffs(cm) - 1;
-            const uint32_t n = __ffs(~(cm >> j)) - 1;
+            const uint32_t n = sched.span ? (32u - __clz(cm)) - j : __ffs(~(cm >> j)) - 1;
             if ((cm >> (j + n)) == 0u) {
               j0 = j;
               n0 = n;
@@ -1144,6 +1146,12 @@ bool env_on(const char* name) {
   const char* s = getenv(name);
   return !(s != nullptr && s[0] == '0');
 }
+// CCE_DLOGITS_SPAN=0: dlogits narrows its MMA only to a single run of kept
+// column groups instead of the span of all of them (A/B switch).
+bool dlogits_span() {
+  static const bool v = env_on("CCE_DLOGITS_SPAN");
+  return v;
+}
 bool half_k_enabled() {
   static const bool v = env_on("CCE_GRAD_E_HALF_K");
   return v;
@@ -1295,6 +1303,7 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
            a.counters ? a.counters + 0 : nullptr, raster_group(a.N * a.D * 2)};
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
+  sc.span = dlogits_span() ? 1 : 0;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
