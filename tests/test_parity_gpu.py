@@ -279,6 +279,18 @@ def test_ragged_shapes(N, D, V, dtype):
     check(run(e, c, t), oracle(e, c, t), dtype)
 
 
+@pytest.mark.parametrize("D", [192, 576, 2112])
+def test_grad_e_tile_pairs_past_d(D):
+    """grad_e runs as pairs of 256-column output tiles; with D = 192, 576 or
+    2112 the last pair reaches past D (its second tile wholly, or its first
+    tile partly): the B box there is zero-filled, and the tiles' columns past
+    D are neither stored nor sent.  bf16, 10% ignored rows, against the
+    float64 oracle."""
+    e, c, t, _ = small(300, D, 5000, torch.bfloat16, seed=D, ignore=0.1)
+    t[0] = 4999
+    check(run(e, c, t), oracle(e, c, t), torch.bfloat16)
+
+
 def test_multichunk_fp16_bias_ragged(monkeypatch):
     """N = 4200 rows (not a multiple of 128) with 16384-row vocabulary chunks
     (forced through CCE_BWD_CHUNK_ROWS; the default rule would take one chunk
