@@ -100,7 +100,7 @@ constexpr int kMaskWarps = 8;
 constexpr int kTilesPer128 = 128 / kStatTile;
 static_assert(kMaskTiles % kTilesPer128 == 0, "whole 128-column tiles per round");
 
-__global__ void __launch_bounds__(kMaskWarps * 32)
+__global__ void __launch_bounds__(kMaskWarps * 32, 4)
 block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ lse,
                   const int32_t* __restrict__ targets, const float* __restrict__ d_nll, int64_t N,
                   int64_t V, int64_t v_offset, float log_eps, int no_filter, uint8_t* __restrict__ keep,
@@ -116,41 +116,37 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
   const int64_t i = blockIdx.y;  // row block
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kRowsPerLane = kRowBlock / 32;
+  // Per row: its LSE, whether it is live, and the statistics tile holding its
+  // target in this call's vocabulary range (-1: none), kept in few registers
+  // so that four blocks fit on an SM.
   float L[kRowsPerLane];
-  int64_t tl[kRowsPerLane];
+  int tt[kRowsPerLane];
   bool live[kRowsPerLane];
-  const float* tm[kRowsPerLane];
+  const float* tm0 = tile_max + i * kRowBlock + lane;  // + 32 u + j N: row lane + 32 u, tile j
 #pragma unroll
   for (int u = 0; u < kRowsPerLane; ++u) {
     const int64_t row = i * kRowBlock + lane + 32 * u;
     live[u] = row < N && d_nll[row] != 0.f;  // rows with a zero cotangent contribute nothing
     L[u] = live[u] ? lse[row] : 0.f;
-    tl[u] = live[u] ? (int64_t)targets[row] - v_offset : -1;
-    tm[u] = tile_max + (live[u] ? row : 0);
+    const int64_t tl = live[u] ? (int64_t)targets[row] - v_offset : -1;
+    tt[u] = (tl >= 0 && tl < V) ? (int)(tl / kStatTile) : -1;
   }
   constexpr int kTilesPerWarp = kMaskTiles / kMaskWarps;
   int skipped = 0, total = 0;
   const int64_t tile0 = (int64_t)blockIdx.x * kMaskRounds * kMaskTiles;
-  // All of this warp's tile maxima of a round are loaded before any is
-  // tested, and the next round's are loaded before this round's are tested,
-  // so two rounds of loads are in flight at a time.
-  float x[kTilesPerWarp][kRowsPerLane], xn[kTilesPerWarp][kRowsPerLane];
-  auto load_round = [&](int r, float (&dst)[kTilesPerWarp][kRowsPerLane]) {
-    const int64_t base = tile0 + (int64_t)r * kMaskTiles;
-#pragma unroll
-    for (int q = 0; q < kTilesPerWarp; ++q) {
-      const int64_t j = base + warp + q * kMaskWarps;
-#pragma unroll
-      for (int u = 0; u < kRowsPerLane; ++u)
-        dst[q][u] = (r < kMaskRounds && live[u] && j < nVt) ? __ldg(tm[u] + j * N) : -INFINITY;
-    }
-  };
-  load_round(0, x);
 #pragma unroll 1
   for (int r = 0; r < kMaskRounds; ++r) {
     const int64_t base = tile0 + (int64_t)r * kMaskTiles;
     if (base >= nVt) break;
-    load_round(r + 1, xn);
+    // all of this warp's tile maxima of the round are loaded before any is
+    // tested, so the loads overlap
+    float x[kTilesPerWarp][kRowsPerLane];
+#pragma unroll
+    for (int q = 0; q < kTilesPerWarp; ++q) {
+      const int64_t j = base + warp + q * kMaskWarps;
+#pragma unroll
+      for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = (live[u] && j < nVt) ? __ldg(tm0 + 32 * u + j * N) : -INFINITY;
+    }
 #pragma unroll
     for (int q = 0; q < kTilesPerWarp; ++q) {
       const int w = warp + q * kMaskWarps;
@@ -159,10 +155,7 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
       bool k = false;
 #pragma unroll
       for (int u = 0; u < kRowsPerLane; ++u) {
-        if (live[u]) {
-          const bool hit = tl[u] >= j * kStatTile && tl[u] < (j + 1) * kStatTile && tl[u] < V;
-          k = k || no_filter || hit || (x[q][u] - L[u] >= log_eps);
-        }
+        if (live[u]) k = k || no_filter || tt[u] == (int)j || (x[q][u] - L[u] >= log_eps);
       }
       k = __any_sync(0xffffffffu, k);
       if (lane == 0) {
@@ -172,10 +165,6 @@ block_mask_kernel(const float* __restrict__ tile_max, const float* __restrict__ 
       ++total;
       skipped += k ? 0 : 1;
     }
-#pragma unroll
-    for (int q = 0; q < kTilesPerWarp; ++q)
-#pragma unroll
-      for (int u = 0; u < kRowsPerLane; ++u) x[q][u] = xn[q][u];
   }
   if (skip_stats && lane == 0 && total) {
     atomicAdd(&cnt[0], skipped);
