@@ -134,6 +134,7 @@ struct BwdPlan {
   size_t keep_t_bytes;
   int splits;            // CUDA-core path: K splits of grad_e (partials part_bytes)
   size_t part_bytes;
+  size_t list_bytes;     // tensor-core path: the dlogits live-tile lists of every chunk
 };
 
 bool tc_candidate(int dtype, int64_t D) { return dtype != CCE_F32 && D % 8 == 0; }
@@ -146,6 +147,17 @@ int64_t target_chunk_rows() {
   const char* s = getenv("CCE_BWD_CHUNK_ROWS");
   const long long r = s ? atoll(s) : 0;
   return r >= 256 ? (int64_t)r : kDlTargetRows;
+}
+
+// CCE_DL_LIST=0 in the environment: the dlogits GEMM claims every tile id and
+// passes over the dead ones instead of claiming from a list of live tiles
+// (an A/B switch; read once, since it sizes the workspace).
+bool dl_list_enabled() {
+  static const bool v = [] {
+    const char* s = getenv("CCE_DL_LIST");
+    return !(s != nullptr && s[0] == '0');
+  }();
+  return v;
 }
 
 BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, bool tc) {
@@ -183,8 +195,11 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
   if (!(flags & CCE_NEED_DE)) p.acc_bytes = 0;
   else if (tc) p.acc_bytes = align_up(2 * (size_t)N * (size_t)D * 4);
   else p.acc_bytes = (flags & CCE_DE_F32) ? 0 : align_up((size_t)N * (size_t)D * 4);
-  // three tile counters per vocabulary chunk for the dynamically scheduled kernels
-  p.counter_bytes = align_up((size_t)cce::ceil_div(V > 0 ? V : 1, vc) * 3 * sizeof(int));
+  // four counters per vocabulary chunk: the tile claims of the three
+  // dynamically scheduled kernels and the dlogits live-tile count
+  const int64_t nch = cce::ceil_div(V > 0 ? V : 1, vc);
+  p.counter_bytes = align_up((size_t)nch * 4 * sizeof(int));
+  p.list_bytes = (tc && dl_list_enabled()) ? align_up((size_t)nch * (size_t)cce::tc_dlogits_list_len(nrow, vc) * sizeof(int)) : 0;
   p.scale_bytes = (tc && dtype == CCE_F16) ? kAlign : 0;  // {s, 1/s} for fp16 dlogits
   p.splits = (!tc && (flags & CCE_NEED_DE)) ? cce::simt_grad_e_splits(N, D, vc) : 1;
   p.part_bytes = p.splits > 1 ? align_up((size_t)p.splits * (size_t)N * (size_t)D * 4) : 0;
@@ -192,7 +207,8 @@ BwdPlan plan_backward(int64_t N, int64_t D, int64_t V, int dtype, int flags, boo
 }
 
 size_t plan_bytes(const BwdPlan& p) {
-  return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes + p.keep_t_bytes + p.part_bytes;
+  return p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes + p.scale_bytes + p.keep_t_bytes + p.part_bytes +
+         p.list_bytes;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -707,6 +723,9 @@ static int backward_impl(const void* e, const void* c, const CceQuantHead* qh, c
   float* part = p.part_bytes ? (float*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes +
                                         p.scale_bytes + p.keep_t_bytes)
                              : nullptr;
+  int* dl_lists = p.list_bytes ? (int*)(ws + p.keep_bytes + p.dl_bytes + p.acc_bytes + p.counter_bytes +
+                                         p.scale_bytes + p.keep_t_bytes + p.part_bytes)
+                               : nullptr;
   char* cbuf[2] = {nullptr, nullptr};  // a quantised head's expanded chunks
   if (qh) {
     cbuf[0] = ws + plan_bytes(p);
@@ -720,6 +739,8 @@ static int backward_impl(const void* e, const void* c, const CceQuantHead* qh, c
                                         (flags & CCE_NO_FILTER) != 0, keep, keep_t, p.keep_t_ld, skip_stats, s),
                  "cce_backward mask");
   if (need_db) CCE_CUDA_CHECK(cudaMemsetAsync(grad_bias, 0, (size_t)V * sizeof(float), s), "memset grad_bias");
+  if (dl_lists)
+    CCE_CUDA_CHECK(cce::tc_dlogits_lists(keep, N, D, V, p.vc, dl_lists, counters, s), "cce_backward dlogits lists");
 
   cce::BwdChunkArgs a{e, c, nullptr, bias, bias_dtype, targets, lse, d_nll, keep, keep_t, p.keep_t_ld, N, D, V,
                       v_offset, dtype, 0, 0, p.vc, dl, need_db ? grad_bias : nullptr, nullptr, scale};
@@ -746,7 +767,8 @@ static int backward_impl(const void* e, const void* c, const CceQuantHead* qh, c
     a.vc0 = ch * p.vc;
     a.vc_len = (V - a.vc0) < p.vc ? (V - a.vc0) : p.vc;
     const bool last = ch == nchunks - 1;
-    a.counters = counters + 3 * ch;
+    a.counters = counters + 4 * ch;
+    a.dl_list = dl_lists ? dl_lists + ch * cce::tc_dlogits_list_len(N, p.vc) : nullptr;
     // dlogits(ch) on `s` overwrites the buffer grad_e / grad_c of chunk ch-1 read
     if (p.tc && ch > 0) {
       CCE_CUDA_CHECK(cudaStreamWaitEvent(s, ss->ev_e, 0), "cce_backward join");

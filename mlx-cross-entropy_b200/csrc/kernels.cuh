@@ -56,8 +56,10 @@ struct BwdChunkArgs {
   int64_t vc_ld;         // row stride of the dlogits buffer (elements)
   void* dlogits;         // [N][vc_ld], fp32 (SIMT path) or 16-bit (tensor-core path)
   float* grad_bias;      // [V] fp32 or nullptr
-  int* counters;         // 3 zeroed tile counters of this chunk (dlogits, grad_e, grad_c) or nullptr
+  int* counters;         // 4 zeroed counters of this chunk (dlogits, grad_e, grad_c tile claims; the
+                         // dlogits live-tile count) or nullptr
   const float* scale;    // fp16 tensor-core path: {s, 1/s} with s = 2^ceil(log2 max|d_nll|); else nullptr
+  const int* dl_list = nullptr;  // the chunk's live dlogits tiles (tc_dlogits_lists), count in counters[3]
 };
 
 // ---- auxiliary kernels (aux_kernels.cu) ----
@@ -108,6 +110,12 @@ int tc_read_status(bool reset);
 int tc_read_mma_flops(uint64_t* out4, bool reset);
 cudaError_t tc_forward(const FwdArgs& a, cudaStream_t stream);
 cudaError_t tc_dlogits(const BwdChunkArgs& a, cudaStream_t stream);
+// Lists, per vocabulary chunk of vc rows, the dlogits work units with a kept
+// block in schedule order: chunk ch's ids at lists + ch * tc_dlogits_list_len(N, vc),
+// their count in counters[4 ch + 3] (zeroed before).  One block per chunk.
+int64_t tc_dlogits_list_len(int64_t N, int64_t vc);
+cudaError_t tc_dlogits_lists(const uint8_t* keep, int64_t N, int64_t D, int64_t V, int64_t vc, int* lists,
+                             int* counters, cudaStream_t stream);
 // acc2[2][N][D] fp32: each output tile's two K halves of this chunk are
 // stored (accumulate = false) or added into slabs 0 and 1; grad_e is
 // acc2[0] + acc2[1] after the last chunk (launch_sum2_f32).  With `push`

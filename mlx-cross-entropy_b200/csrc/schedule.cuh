@@ -25,6 +25,8 @@ struct Sched {
   int group;     // grouped raster: blocks of the fast dimension per group (<= 0: all)
   int ksplit;    // K splits per output tile (<= 1: none); split s is its own work unit
   int span;      // K-major B: one MMA over the span of a tile's kept column groups
+  const int* list;        // claims index this list of unit ids (nullptr: claim = unit id)
+  const int* list_count;  // its length, read at the kernel's start
   __host__ __device__ __forceinline__ int splits() const { return ksplit > 1 ? ksplit : 1; }
   __host__ __device__ __forceinline__ int units() const { return num_m * num_n * splits(); }
   // Unit id -> (mb, nb, ks).  All units of split 0 come first, then split 1, ...
@@ -63,7 +65,7 @@ struct Sched {
 
 // Fast-dimension group size: all blocks when that operand fits comfortably in
 // L2 (it is then read from DRAM once however the tiles are ordered), else 16.
-inline int raster_group(int64_t fast_operand_bytes) {
+__host__ __device__ inline int raster_group(int64_t fast_operand_bytes) {
   return fast_operand_bytes <= (40ll << 20) ? 0 : 16;
 }
 

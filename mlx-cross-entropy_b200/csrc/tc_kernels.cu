@@ -77,6 +77,23 @@ constexpr int kPushWaitCode = 8;  // status code: a push unit's epilogue threads
 // costs on its own, so longer runs load the whole tile in one box.
 constexpr uint32_t kNarrowMaxGroups = 2;
 constexpr uint32_t B32_BYTES = kStatTile * BK * 2;  // 4 KB: 32 rows x 128 bytes
+// Narrow tiles two K-blocks per stage (kNarrowB epilogues with `dbl` set):
+// the stage's A slot holds A(kb); its B slot holds A(kb + 1) in the first
+// A_BYTES, then the live B rows of kb and of kb + 1, kNarrowMaxGroups boxes
+// each -- half the load round trips of a tile that fills a third of a stage.
+constexpr uint32_t kDblB0 = A_BYTES;                                 // B(kb) in the B slot
+constexpr uint32_t kDblB1 = A_BYTES + kNarrowMaxGroups * B32_BYTES;  // B(kb + 1)
+static_assert(kDblB1 + kNarrowMaxGroups * B32_BYTES <= B_BYTES, "two narrow K-blocks per stage");
+
+// The single run of kept column groups [j, j + n) of a tile's column mask cm
+// whose B rows are loaded alone (n <= kNarrowMaxGroups); false for a full or
+// empty mask or more than one run.
+__device__ __forceinline__ bool narrow_run(uint32_t cm, uint32_t& j, uint32_t& n) {
+  if (cm == kAllGroups || cm == 0u) return false;
+  j = __ffs(cm) - 1;
+  n = __ffs(~(cm >> j)) - 1;
+  return (cm >> (j + n)) == 0u && n <= kNarrowMaxGroups;
+}
 // Half K-blocks (kHalfK epilogues): a K-block whose only kept statistics tile
 // is one of its two 32-row halves loads that half alone -- A as a 128 x 32
 // box in the 64-byte swizzle (SW64 K-major), B as a 3-D box of 32 K-rows x
@@ -200,6 +217,8 @@ struct Stager {
 template <typename TB>  // bias element type; void = no bias
 struct FwdEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kPairLd = false;  // the epilogue reads TMEM two 32-column chunks at a time
+  __device__ __forceinline__ bool pair_ld() const { return false; }
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 0;  // slot in g_mma_cols
@@ -287,6 +306,8 @@ struct FwdEpi {
 template <typename T, typename TB>
 struct DlogitsEpi {
   static constexpr bool kNarrowB = true;  // B rows loaded for a tile's live column run only
+  static constexpr bool kPairLd = false;  // the epilogue reads TMEM two 32-column chunks at a time
+  __device__ __forceinline__ bool pair_ld() const { return false; }
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 1;  // slot in g_mma_cols
@@ -301,6 +322,7 @@ struct DlogitsEpi {
   int64_t mask_ld;          // nVt
   int mask_rows, mask_cols; // nRb, statistics tiles in the chunk
   int64_t N, V, v_offset, vc0, vc_end, ld;
+  int dbl = 0;     // narrow tiles load two K-blocks per stage (kDblB0)
 
   struct State {
     int64_t row, tl, col0;
@@ -404,6 +426,8 @@ struct DlogitsEpi {
 // unit raises the `pushed` flag on every rank.  The slabs are not written.
 struct GradEEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kPairLd = false;  // the epilogue reads TMEM two 32-column chunks at a time
+  __device__ __forceinline__ bool pair_ld() const { return false; }
   static constexpr bool kHalfK = true;  // half K-blocks loaded alone when half_k is set
   static constexpr bool kWideCapable = true;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 2;  // slot in g_mma_cols
@@ -556,6 +580,7 @@ struct GradEEpi {
 template <typename T>
 struct GradCEpi {
   static constexpr bool kNarrowB = false;  // B rows loaded for a tile's live column run only
+  static constexpr bool kPairLd = true;   // the epilogue reads TMEM two 32-column chunks at a time
   static constexpr bool kHalfK = false;  // half K-blocks loaded alone (see A_HALF_BYTES)
   static constexpr bool kWideCapable = false;  // may run as wide units (see GradEEpi)
   static constexpr int kKind = 3;  // slot in g_mma_cols
@@ -565,6 +590,8 @@ struct GradCEpi {
   int64_t mask_ld;          // words per table row
   int mask_rows, mask_cols; // M tiles in the chunk, nRb
   int64_t rows, D;
+  int pair = 1;             // TMEM read two chunks per wait (kPairLd), else one
+  __device__ __forceinline__ bool pair_ld() const { return pair != 0; }
 
   struct State {
     int64_t row, col0;
@@ -748,6 +775,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // (Epi::skip_unit) is passed over here and never reaches the MMA and
       // epilogue warps.  (Claiming several ids per atomic after dead units
       // measured slower: live tiles then bunch up on a few SMs.)
+      // With a unit list (sched.list) a claim k is list entry k, a unit with
+      // work; the entry is read when the claim is taken up.
+      const int num_claims = sched.list ? min(*sched.list_count, num_tiles) : num_tiles;
       int next = sched.counter ? atomicAdd(sched.counter, 1) : (int)blockIdx.x;
       int sidx = 0;  // static schedule: claims made
       auto advance = [&]() {
@@ -758,8 +788,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait(rempty + slot, ((i / RING) & 1) ^ 1u, 5)) break;
         int tile = -1;
         int mb = 0, nb = 0, ks = 0, kb0 = 0, kb1 = 0;
-        while (next < num_tiles) {
-          const int u = next;
+        while (next < num_claims) {
+          const int u = sched.list ? __ldg(sched.list + next) : next;
           sched.coords(u, mb, nb, ks);
           sched.krange(ks, kb0, kb1);
           const bool skip = epi.skip_unit(mk, mb, nb, kb0, kb1);
@@ -777,24 +807,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // short run of live 32-column groups [nj0, nj0 + nn0) -- the rows
         // the MMA of this tile reads (see the MMA issuer)
         uint32_t nj0 = 0, nn0 = kGroups;
+        bool dbl = false;  // two K-blocks per stage (see kDblB0)
         if constexpr (Epi::kNarrowB && !B_MN) {
-          const uint32_t cm = epi.col_mask(mk, mb, nb);
-          if (cm != kAllGroups) {
-            const uint32_t j = __ffs(cm) - 1;
-            const uint32_t n = __ffs(~(cm >> j)) - 1;
-            if ((cm >> (j + n)) == 0u && n <= kNarrowMaxGroups) {
-              nj0 = j;
-              nn0 = n;
-            }
+          uint32_t j, n;
+          if (narrow_run(epi.col_mask(mk, mb, nb), j, n)) {
+            nj0 = j;
+            nn0 = n;
+            dbl = epi.dbl != 0;
           }
         }
         const uint32_t tx_bytes = A_BYTES + (nn0 < (uint32_t)kGroups ? nn0 * B32_BYTES : B_BYTES);
+        const int kstep = dbl ? 2 : 1;
         bool ok = true;
-        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
+        for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + kstep, kb1)) {
           if (!mbar_wait(empty + stage, phase ^ 1u, 1)) { ok = false; break; }
           uint8_t* a = sA + stage * A_BYTES;
           uint8_t* b = sB + stage * B_BYTES;
           const int k0 = kb * BK;
+          if constexpr (Epi::kNarrowB && !B_MN) {
+            if (dbl) {
+              const bool two = kb + 1 < kb1;
+              mbar_arrive_expect_tx(full + stage, (two ? 2u : 1u) * tx_bytes);
+              tma_load_2d(a, &tmA, full + stage, k0, mb * BM);
+              for (uint32_t g = 0; g < nn0; ++g)
+                tma_load_2d(b + kDblB0 + g * B32_BYTES, &tmBalt, full + stage, k0, nb * BN + (int)((nj0 + g) * kStatTile));
+              if (two) {
+                tma_load_2d(b, &tmA, full + stage, k0 + BK, mb * BM);
+                for (uint32_t g = 0; g < nn0; ++g)
+                  tma_load_2d(b + kDblB1 + g * B32_BYTES, &tmBalt, full + stage, k0 + BK,
+                              nb * BN + (int)((nj0 + g) * kStatTile));
+              }
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
+            }
+          }
           if constexpr (Epi::kWideCapable) {
             if (epi.wide) {
               // one statistics tile of K for the tile pair nb = 2 np, 2 np + 1
@@ -931,6 +980,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // shared memory and measured slower.)  sched.span = 0 narrows only a
         // single run of kept groups.
         uint32_t j0 = 0, n0 = kGroups;
+        bool dbl = false;  // the producer's two-K-blocks-per-stage layout (kDblB0)
         if constexpr (!B_MN) {
           const uint32_t cm = epi.col_mask(mk, mb, nb);
           if (cm != kAllGroups && cm != 0u) {
@@ -941,12 +991,50 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               n0 = n;
             }
           }
+          if constexpr (Epi::kNarrowB) {
+            uint32_t j, n;
+            dbl = epi.dbl != 0 && narrow_run(cm, j, n);  // then (j, n) == (j0, n0)
+          }
         }
         const uint32_t idesc0 = idesc_with_n(idesc, kStatTile * n0);
         const uint32_t d0 = d_tmem + kStatTile * j0;
         const uint32_t boff = (kStatTile * 128u * j0) >> 4;
         bool ok = true;
         uint32_t fresh = 1;  // the tile's first MMA overwrites the accumulator
+        if constexpr (Epi::kNarrowB && !B_MN) {
+          if (dbl) {
+            for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 2, kb1)) {
+              const bool two = kb + 1 < kb1;
+              mma_cols += (unsigned long long)((two ? 2 : 1) * (BK / 16) * kStatTile * n0);
+              if (!mbar_wait(full + stage, phase, 3)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t sb = smem_u32(sB + stage * B_BYTES);
+              const uint64_t ad = adesc0 + (uint64_t)((stage * A_BYTES) >> 4);
+              const uint64_t bd = smem_desc(sb + kDblB0, 16, 1024);
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k) {
+                mma_f16(d0, ad + k * a_kstep, bd + k * b_kstep, idesc0, fresh ^ 1u);
+                fresh = 0;
+              }
+              if (two) {
+                const uint64_t ad1 = smem_desc(sb, 16, 1024);
+                const uint64_t bd1 = smem_desc(sb + kDblB1, 16, 1024);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) mma_f16(d0, ad1 + k * a_kstep, bd1 + k * b_kstep, idesc0, 1u);
+              }
+              mma_commit(empty + stage);
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            mma_commit(tfull + acc);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+            continue;
+          }
+        }
         for (int kb = epi.next_kb(mk, mb, nb, kb0, kb1); kb < kb1; kb = epi.next_kb(mk, mb, nb, kb + 1, kb1)) {
           const uint32_t km = epi.ksub_mask(mk, mb, nb, kb);  // K=16 steps to issue
           mma_cols += (unsigned long long)(__popc(km & 0xFu) * kStatTile * n0);
@@ -1026,6 +1114,35 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if constexpr (Epi::kZeroTiles) zero_tile = !any_kb && epi.zero_shortcut();
         if (zero_tile) {
           if constexpr (Epi::kZeroTiles) epi.zero_tile(st);
+        } else if (Epi::kPairLd && epi.pair_ld() && any_kb) {
+          // two chunks per TMEM wait: the loads of chunks 2p + 2, 2p + 3 are in
+          // flight while chunks 2p, 2p + 1 are processed (every chunk live)
+          uint32_t cur0[32], cur1[32], nxt0[32], nxt1[32];
+          tmem_ld32_issue(tbase, cur0);
+          tmem_ld32_issue(tbase + 32, cur1);
+#pragma unroll 1
+          for (int p = 0; p < BN / 64; ++p) {
+            __syncwarp();
+            tmem_ld_wait(cur0);
+            tmem_ld_wait(cur1);
+            const bool more = p + 1 < BN / 64;
+            if (more) {
+              tmem_ld32_issue(tbase + (2 * p + 2) * 32, nxt0);
+              tmem_ld32_issue(tbase + (2 * p + 3) * 32, nxt1);
+            }
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur0[j]);
+            epi.chunk(st, 2 * p, v, sg);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur1[j]);
+            epi.chunk(st, 2 * p + 1, v, sg);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              cur0[j] = nxt0[j];
+              cur1[j] = nxt1[j];
+            }
+          }
         } else {
           // the TMEM load of chunk c + 1 is in flight while chunk c is processed
           uint32_t cur[32], nxt[32];
@@ -1158,6 +1275,16 @@ bool half_k_enabled() {
 }
 bool wide_enabled() {
   static const bool v = env_on("CCE_GRAD_E_WIDE");
+  return v;
+}
+// CCE_GRAD_C_PAIR_LD=0: the grad_c epilogue reads TMEM one 32-column chunk per wait.
+bool grad_c_pair_ld() {
+  static const bool v = env_on("CCE_GRAD_C_PAIR_LD");
+  return v;
+}
+// CCE_DLOGITS_DOUBLE_K=0: narrow dlogits tiles load one K-block per stage.
+bool dlogits_double_k() {
+  static const bool v = env_on("CCE_DLOGITS_DOUBLE_K");
   return v;
 }
 
@@ -1293,6 +1420,81 @@ cudaError_t fwd_launch(const FwdArgs& a, cudaStream_t s) {
   return launch_gemm<false, false>(tmA, tmB, tmA, tmB, tmC, sc, epi, bf16, s);
 }
 
+// The dlogits schedule of a chunk of vc_len rows (also the list builder's).
+__host__ __device__ Sched dl_sched(int64_t N, int64_t D, int64_t vc_len, int* counter) {
+  return Sched{(int)ceil_div(N, BM), (int)ceil_div(vc_len, BN), (int)ceil_div(D, BK), 1, 0, 0,
+               counter, raster_group(N * D * 2)};
+}
+
+// One block per vocabulary chunk: thread t checks a run of consecutive unit
+// ids (a tile's 8 mask bytes in one 8-byte load where they are aligned), a
+// block-wide scan gives each run its place, so the list keeps the schedule
+// order.
+__global__ void __launch_bounds__(1024) dl_list_kernel(const uint8_t* keep, int64_t N, int64_t D, int64_t V,
+                                                         int64_t vc, int* lists, int64_t list_len, int* counters) {
+  static_assert(kGroups == 8, "one 8-byte mask load per tile");
+  __shared__ int warp_tot[32];
+  const int ch = blockIdx.x;
+  const int64_t vc0 = (int64_t)ch * vc;
+  const int64_t vlen = min(vc, V - vc0);
+  const Sched sc = dl_sched(N, D, vlen, nullptr);
+  const int units = sc.units();
+  const int64_t nvt = ceil_div(V, (int64_t)kStatTile);
+  const int64_t t0 = vc0 / kStatTile;
+  const int tiles = (int)ceil_div(vlen, (int64_t)kStatTile);  // the chunk's statistics tiles
+  const bool wide = ((nvt | t0) & 7) == 0 && (reinterpret_cast<uintptr_t>(keep) & 7) == 0;
+  const int per = (units + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int u0 = min(units, (int)threadIdx.x * per), u1 = min(units, u0 + per);
+  auto live = [&](int u) {
+    int mb, nb, ks;
+    sc.coords(u, mb, nb, ks);
+    const uint8_t* row = keep + (int64_t)mb * nvt + t0;
+    const int g0 = kGroups * nb, g1 = min(g0 + kGroups, tiles);
+    if (wide && g1 - g0 == kGroups) return __ldg(reinterpret_cast<const unsigned long long*>(row + g0)) != 0ull;
+    bool any = false;
+    for (int g = g0; g < g1; ++g) any |= __ldg(row + g) != 0;
+    return any;
+  };
+  // pass 1: count (live bits of the first 32 units kept in a register)
+  uint32_t bits = 0;
+  int cnt = 0;
+#pragma unroll 8
+  for (int i = 0; i < per; ++i) {
+    const int u = u0 + i;
+    if (u < u1 && live(u)) {
+      ++cnt;
+      if (i < 32) bits |= 1u << i;
+    }
+  }
+  // exclusive scan of cnt over the block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (int)(blockDim.x >> 5);
+    int w = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) warp_tot[lane] = w;  // inclusive over warps
+    if (lane == nw - 1) counters[4 * ch + 3] = w;
+  }
+  __syncthreads();
+  // pass 2: write the ids
+  int pos = incl - cnt + (warp > 0 ? warp_tot[warp - 1] : 0);
+  int* list = lists + (int64_t)ch * list_len;
+  for (int i = 0; i < per && u0 + i < u1; ++i)
+    if (i < 32 ? ((bits >> i) & 1u) != 0 : live(u0 + i)) list[pos++] = u0 + i;
+}
+
 template <typename T, typename TB>
 cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const bool bf16 = a.dtype == CCE_BF16;
@@ -1300,14 +1502,18 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
   const void* cchunk = a.c_chunk;
   if (!make_tmap(&tmA, a.e, bf16, a.D, a.N, a.D, BK, BM)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB, cchunk, bf16, a.D, a.vc_len, a.D, BK, BN)) return cudaErrorInvalidValue;
-  Sched sc{(int)ceil_div(a.N, BM), (int)ceil_div(a.vc_len, BN), (int)ceil_div(a.D, BK), 1, 0, 0,
-           a.counters ? a.counters + 0 : nullptr, raster_group(a.N * a.D * 2)};
+  Sched sc = dl_sched(a.N, a.D, a.vc_len, a.counters ? a.counters + 0 : nullptr);
+  if (a.dl_list != nullptr && a.counters != nullptr) {
+    sc.list = a.dl_list;
+    sc.list_count = a.counters + 3;
+  }
   const int64_t vc_end = (a.vc0 + a.vc_len) < a.V ? (a.vc0 + a.vc_len) : a.V;
   sc.span = dlogits_span() ? 1 : 0;
   DlogitsEpi<T, TB> epi{a.targets, a.lse, a.d_nll, a.bias, static_cast<T*>(a.dlogits), a.grad_bias,
                         a.scale, a.keep + a.vc0 / kStatTile, ceil_div(a.V, kStatTile),
                         (int)ceil_div(a.N, kRowBlock), (int)ceil_div(a.vc_len, kStatTile),
                         a.N, a.V, a.v_offset, a.vc0, vc_end, a.vc_ld};
+  epi.dbl = dlogits_double_k() ? 1 : 0;
   CUtensorMap tmC, tmB32;
   if (!make_tmap_out(&tmC, a.dlogits, a.dtype, a.vc_len, a.N, a.vc_ld)) return cudaErrorInvalidValue;
   if (!make_tmap(&tmB32, cchunk, bf16, a.D, a.vc_len, a.D, BK, kStatTile)) return cudaErrorInvalidValue;
@@ -1315,6 +1521,16 @@ cudaError_t dl_launch(const BwdChunkArgs& a, cudaStream_t s) {
 }
 
 }  // namespace
+
+int64_t tc_dlogits_list_len(int64_t N, int64_t vc) { return ceil_div(N, (int64_t)BM) * ceil_div(vc, (int64_t)BN); }
+
+cudaError_t tc_dlogits_lists(const uint8_t* keep, int64_t N, int64_t D, int64_t V, int64_t vc, int* lists,
+                             int* counters, cudaStream_t s) {
+  if (N == 0 || V == 0) return cudaSuccess;
+  const int64_t nch = ceil_div(V, vc);
+  dl_list_kernel<<<(unsigned)nch, 1024, 0, s>>>(keep, N, D, V, vc, lists, tc_dlogits_list_len(N, vc), counters);
+  return cudaGetLastError();
+}
 
 cudaError_t tc_forward(const FwdArgs& a, cudaStream_t s) {
   if (a.N == 0 || a.V == 0) return cudaSuccess;
@@ -1400,6 +1616,7 @@ cudaError_t grad_c_launch(const BwdChunkArgs& a, void* grad_c, cudaStream_t s) {
                   a.keep_t + (a.vc0 / 128) * a.keep_t_ld, a.keep_t_ld,
                   (int)ceil_div(a.vc_len, (int64_t)128), (int)ceil_div(a.N, kRowBlock),
                   a.vc_len, a.D};
+  epi.pair = grad_c_pair_ld() ? 1 : 0;
   CUtensorMap tmC;
   if (!make_tmap_out(&tmC, static_cast<uint16_t*>(grad_c) + a.vc0 * a.D, a.dtype, a.D, a.vc_len, a.D))
     return cudaErrorInvalidValue;

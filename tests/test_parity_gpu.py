@@ -363,6 +363,33 @@ def test_filter_matches_same_granularity_oracle_and_no_filter_is_exact():
     check(got_exact, ref, torch.bfloat16, grad_tol=1e-2)
 
 
+@pytest.mark.parametrize("D", [136, 520])
+def test_sparse_narrow_tiles_odd_k_blocks(D, monkeypatch):
+    """Peaked logits (most 128 x 32 blocks rejected) with an odd number of
+    64-column K-blocks, ragged N and V and four vocabulary chunks (the last
+    one 856 rows, its statistics tiles not a multiple of 8): dlogits tiles
+    with one or two kept 32-column groups load two K-blocks per pipeline
+    stage (the last stage one), and dlogits claims its tiles from the
+    per-chunk live-tile lists.  Loss and gradients match the oracle filtered
+    at the same granularity (rule of csrc/cce/cce.metal:190-204)."""
+    monkeypatch.setenv("CCE_BWD_CHUNK_ROWS", "2048")
+    e, c, t, _, _, _ = synthetic.make_inputs(3, N=300, V=7000, D=D)
+    dev = _dev()
+    stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    got = run(e, c, t, skip_stats=stats)
+    ref = oracle(e, c, t)
+    np.testing.assert_allclose(got["loss"], ref["loss"], rtol=1e-3)
+    skipped, total = stats.tolist()
+    assert skipped > 0.5 * total
+    safe, valid = O.sanitize(t.numpy())
+    d = O.d_nll_from_reduction(valid, "mean")
+    fE, fC, _, frac = O.backward_filtered(e.double().numpy(), c.double().numpy(), ref["lse"], safe,
+                                          d, block_rows=128, block_cols=32, skip_zero_rows=True)
+    assert abs(skipped / total - frac) <= 2.0 / total
+    assert O.rel_max_abs(got["dE"], fE) < GRAD_TOL
+    assert O.rel_max_abs(got["dC"], fC) < GRAD_TOL
+
+
 def test_cuda_graph_capture_matches_eager():
     """fwd + bwd through the public API captured in a CUDA graph (side-stream
     fork/join and workspace memsets included) and replayed on new input values
